@@ -170,6 +170,17 @@ class ClockSampler:
                 "power_w_max": max(r["power"] for r in rows)}
 
 
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
+
+
 # ---------------------------------------------------------------------------- reference arm
 def run_reference(args, seq):
     """CPU restatement of the reference path, timed on a bounded sample."""
@@ -181,6 +192,10 @@ def run_reference(args, seq):
     w = workload(seq)
     S, D = w["S"], w["D"]
     nb = math.ceil(S / 64)
+    # every host core this process may run on, whatever OMP_NUM_THREADS torchrun exported
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    torch.set_num_threads(threads)
+    threads = oracle.set_threads(threads)
     # sample: one Q head (and its KV head) of the layer, the heaviest `tiles` tiles
     tiles = args.ref_tiles
     t0, t1 = max(0, nb - tiles), nb
@@ -209,7 +224,6 @@ def run_reference(args, seq):
         times.append(time.perf_counter() - a)
     sec = sum(times) / len(times)
     value = sample_flops / sec / 1e12
-    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
     sample = (f"1 of {w['Hq']} Q heads, tiles {t0}-{t1 - 1} of {nb} (the heaviest), S={S}: block summary of its KV head, "
               f"tile scores, ranking + sigma, attention over the selected blocks")
     line = {"metric": METRIC, "impl": "reference", "value": round(value, 6), "unit": UNIT, "n_gpus": args.gpus,
@@ -217,7 +231,8 @@ def run_reference(args, seq):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded N(0,1), bf16-rounded)",
             "config": config_for(seq, args.gpus, getattr(args, "split", "auto")),
-            "cpu_baseline": {"value": round(value, 6), "unit": UNIT, "cores": cores, "kind": "port",
+            "cpu_baseline": {"value": round(value, 6), "unit": UNIT, "cores": threads, "threads": threads,
+                             "host_cpus": os.cpu_count(), "cpu_model": cpu_model(), "kind": "port",
                              "sample": sample},
             "e2e": {"value": round(value, 6), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "projected_full_layer_ms": round(sec * 1e3 * (dense_equiv_flops(w["Hq"], S, D) / sample_flops), 1)}

@@ -8,8 +8,8 @@
  *   _block_select_kv_idx_v2(query, key_states, scaling)   src/sparse_attention.py:588-748
  *   block_sparse_attn_v2(q, k, v, kv_idx, scale)          src/triton_block_attn.py:267-298
  * Each entry point below names the part of that path it replaces.  A Python
- * caller binds them with ctypes; the package
- * ugbsa.sparse_attention does exactly that.
+ * caller binds them with ctypes, as the package ugbsa.sparse_attention does
+ * (its ugbsa/_lib.py lists every signature).
  *
  * Conventions
  *  - Every function returns an int status: 0 (UGBSA_OK) or a UGBSA_ERR_* code.
@@ -21,7 +21,7 @@
  *  - Every launch goes to the given cudaStream_t and is asynchronous; no entry
  *    point synchronises the host except ugbsa_read_device_error().
  *  - The library allocates nothing: scratch memory is a caller-supplied
- *    workspace whose size ugbsa_select_workspace_bytes() reports.
+ *    workspace whose size ugbsa_select_workspace_bytes_ex() reports.
  *  - Block size is fixed at 64 tokens (BLOCK / BLOCK_M / BLOCK_N of the
  *    reference, src/sparse_attention.py:51, triton_block_attn.py:267).
  */
@@ -91,7 +91,15 @@ const char *ugbsa_status_string(int status);
  * the router, capped at the block count). */
 int ugbsa_select_budget(const ugbsa_selector_config *cfg, int S, int *k_base, int *kmax);
 
-/* Bytes of scratch memory ugbsa_select needs for this problem. */
+/* Bytes of scratch memory ugbsa_select needs for this problem: exactly what it
+ * lays out for this dtype, head_dim D and KV head count (ugbsa_select returns
+ * UGBSA_ERR_WORKSPACE when given less). */
+size_t ugbsa_select_workspace_bytes_ex(const ugbsa_selector_config *cfg, int dtype, int B, int Hq, int Hkv, int S,
+                                       int D);
+
+/* A bound of ugbsa_select_workspace_bytes_ex over every dtype, head_dim
+ * (<= 256) and KV head count (<= Hq), for callers that size the workspace
+ * before they know those: at least as large as the exact size, often larger. */
 size_t ugbsa_select_workspace_bytes(const ugbsa_selector_config *cfg, int B, int Hq, int S);
 
 /*
@@ -118,7 +126,8 @@ int ugbsa_block_summary(const void *K, int dtype, ugbsa_strides ks, int B, int H
  *   sigma    optional [B, Hq, Qt] fp32 out: per-tile margin after the grain
  *            step (NaN where undefined); NULL to skip.
  *   trigger  optional [B, Hq, Qt] uint8 out: 1 where the tile kept 2*k_base; NULL to skip.
- *   workspace >= ugbsa_select_workspace_bytes(...) bytes of device memory.
+ *   workspace >= ugbsa_select_workspace_bytes_ex(cfg, dtype, B, Hq, Hkv, S, D)
+ *            bytes of device memory.
  */
 int ugbsa_select(const void *Q, int dtype, ugbsa_strides qs, const float *summ_a, const float *summ_b, int B, int Hq,
                  int Hkv, int S, int D, float scale, const ugbsa_selector_config *cfg, int32_t *kv_idx, int kmax,
@@ -130,8 +139,13 @@ int ugbsa_select(const void *Q, int dtype, ugbsa_strides qs, const float *summ_a
  * device, a binding that only holds the tensors it was handed).  No
  * counterpart in the reference, which allocates freely through PyTorch.
  * The scratch comes from a fixed 1 MiB array inside the library (held by every
- * GPU that loads it until exit); problems needing more (B*Hq*ceil(S/64) above
- * about 250K) return UGBSA_ERR_TOO_LARGE.  The array is shared by all calls on
+ * GPU that loads it until exit); problems whose
+ * ugbsa_select_workspace_bytes_ex(cfg, dtype, B, Hq, Hkv, S, D) exceeds it
+ * return UGBSA_ERR_TOO_LARGE.  With bf16 Q and head_dim 64 / 128 / 256 that
+ * size grows with S^2 (the exact tile scores, 4*B*Hq*ceil(S/64)^2 bytes): 28
+ * query / 4 KV heads at head_dim 128 fit up to about 5K tokens, one head up to
+ * about 28K; other dtypes and head dims fit any S the selector accepts at 28
+ * heads.  The array is shared by all calls on
  * a device: calls whose kernels overlap on the GPU race.  The first call on a
  * device looks the array's address up (cudaGetSymbolAddress) and should come
  * before any stream capture.  Same arguments and results as ugbsa_select.
@@ -150,7 +164,8 @@ int ugbsa_select_noalloc(const void *Q, int dtype, ugbsa_strides qs, const float
  *   kmax slots filled (no sentinel yet), sigma_cells [B, Hq, Qt] fp32 and, if
  *   sigma_rowsum is not NULL, its per-tile sum over these heads [B, Qt] fp32
  *   (head order; exact, since the margins are subnormal).  workspace: scratch
- *   of at least ugbsa_select_workspace_bytes(cfg, B, Hq, S) bytes.
+ *   of at least ugbsa_select_workspace_bytes_ex(cfg, dtype, B, Hq, Hkv, S, D)
+ *   bytes (or the looser ugbsa_select_workspace_bytes(cfg, B, Hq, S)).
  * Between the halves the caller combines shards: row grain -> SUM all-reduce of
  *   sigma_rowsum over ranks; cell grain -> all-gather of sigma_cells.
  * ugbsa_select_finish: quantile over all Hq_total heads and sentinel fill of
@@ -187,7 +202,7 @@ int ugbsa_select_finish(const float *sigma_cells, const float *sigma_all, int B,
  *   sigma_rowsum [B, ceil(Sq/64)] are the slice's tiles.  Bf16 Q with head_dim
  *   64, 128 or 256 (the tensor-core scorer) unless the slice is the whole sequence;
  *   otherwise UGBSA_ERR_UNSUPPORTED.  The workspace bound is the unsplit one,
- *   ugbsa_select_workspace_bytes(cfg, B, Hq, S).
+ *   ugbsa_select_workspace_bytes_ex(cfg, dtype, B, Hq, Hkv, S, D).
  * Between the halves the ranks gather the slices' margins into sigma_all
  *   (row grain: [B, ceil(S/64)] head sums in sequence-tile order; cell grain:
  *   all B * Hq * ceil(S/64) cells in any order, the quantile ignores positions).
@@ -216,8 +231,9 @@ int ugbsa_attn_rows(const void *Q, const void *K, const void *V, int dtype, ugbs
 /*
  * Block-sparse causal attention over per-tile kv_idx lists
  * (replaces src/triton_block_attn.py:184-298, _fwd_kernel_v2 + block_sparse_attn_v2).
- *   Q [B, Hq, Sq, D], K/V [B, Hkv, Sk, D] (bf16 or fp16), GQA resolved
- *   inside (no repeat_kv copy).  kv_idx [B, Hq, ceil(Sq/64), kmax] int32,
+ *   Q [B, Hq, Sq, D], K/V [B, Hkv, Sk, D] (bf16 or fp16 on the tensor cores;
+ *   fp32 on CUDA cores with fp32 products and sums, no output peers), GQA
+ *   resolved inside (no repeat_kv copy).  kv_idx [B, Hq, ceil(Sq/64), kmax] int32,
  *   contiguous; entries >= NB (= ceil(Sk/64)) and blocks starting after the
  *   tile's last row are skipped (triton_block_attn.py:231-233).
  *   out [B, Hq, Sq, D] in the input dtype, written through its own strides

@@ -92,8 +92,18 @@ def lib():
         L.oracle_rank_tiles_range.argtypes = [P, I, I, I, ctypes.POINTER(_Cfg), I, I, P, P]
         L.oracle_attn_range.argtypes = ([P, I64, I64, I64, I64] * 3) + [P, I, I, I, I, I, I, I, F, I, I, P]
         L.oracle_decode_scores.argtypes = [P, I64, I64, I64, P, P, I, I, I, I, I, I, F, I, P]
+        L.oracle_set_threads.argtypes = [I]
+        L.oracle_set_threads.restype = None
+        L.oracle_get_threads.argtypes = []
+        L.oracle_get_threads.restype = I
         _lib = L
     return _lib
+
+
+def set_threads(n: int) -> int:
+    """Use n threads in the restatement's parallel regions; returns the count in effect."""
+    lib().oracle_set_threads(int(n))
+    return lib().oracle_get_threads()
 
 
 def _f32(a):
@@ -220,6 +230,82 @@ def sample_step(q, k, v, scale: float, cfg: OracleConfig, t_begin: int, t_end: i
                              ctypes.c_float(scale), t_begin, t_end, _ptr(out))
     assert rc == 0
     return kv, out
+
+
+def sampled_tiles(q, summ, scale: float, cfg: OracleConfig, tiles) -> dict:
+    """Exact tile scores, the ranked kmax slots (before the router's sentinel
+    fill) and the per-tile margin for the listed query tiles of every (b, h) of
+    ``q`` -- the per-tile part of the selection (src/sparse_attention.py:638-707)
+    at sizes where the whole [B,H,Qt,NB] array would not be worth computing.
+    ``summ`` are the summaries of the KV heads ``q``'s heads read (GQA as usual)."""
+    q = _f32(q)
+    B, Hq, S, D = q.shape
+    sa, sb = (summ if cfg.quest else (summ, None))
+    sa = _f32(sa)
+    sb = _f32(sb) if sb is not None else None
+    Hkv = sa.shape[1]
+    nb = math.ceil(S / BLOCK)
+    tiles = [int(t) for t in tiles]
+    ts = np.full((B, Hq, nb, nb), -np.inf, np.float32)
+    L = lib()
+    for t in tiles:
+        rc = L.oracle_tile_scores_range(_ptr(q), Hq * S * D, S * D, D, 1, _ptr(sa), _ptr(sb) if sb is not None else None,
+                                        B, Hq, Hkv, S, D, ctypes.c_float(scale), int(cfg.quest), t, t + 1, _ptr(ts))
+        assert rc == 0
+    _, km = budget(cfg, S)
+    kv = np.full((B, Hq, nb, km), -1, np.int32)
+    sig = np.full((B, Hq, nb), np.nan, np.float32)
+    for t in tiles:
+        rc = L.oracle_rank_tiles_range(_ptr(ts), B, Hq, S, ctypes.byref(cfg.c()), t, t + 1, _ptr(kv), _ptr(sig))
+        assert rc == 0
+    return {"kv_idx": kv[:, :, tiles], "sigma": sig[:, :, tiles], "tile_scores": ts[:, :, tiles]}
+
+
+def attn_tiles(q, k, v, kv_idx, scale: float, tiles) -> np.ndarray:
+    """Attention rows of the listed query tiles (float64 accumulation, slot
+    semantics of triton_block_attn.py:184-264); returns [B, Hq, len(tiles), 64, D]
+    (rows past S are zero).  kv_idx covers every tile [B, Hq, Qt, kmax]."""
+    q, k, v = _f32(q), _f32(k), _f32(v)
+    kv_idx = np.ascontiguousarray(kv_idx, dtype=np.int32)
+    B, Hq, Sq, D = q.shape
+    Hkv, Sk = k.shape[1], k.shape[2]
+    out = np.zeros((B, Hq, Sq, D), np.float32)
+    L = lib()
+    for t in tiles:
+        rc = L.oracle_attn_range(_ptr(q), Hq * Sq * D, Sq * D, D, 1, _ptr(k), Hkv * Sk * D, Sk * D, D, 1,
+                                 _ptr(v), Hkv * Sk * D, Sk * D, D, 1, _ptr(kv_idx), kv_idx.shape[-1], B, Hq, Hkv,
+                                 Sq, Sk, D, ctypes.c_float(scale), int(t), int(t) + 1, _ptr(out))
+        assert rc == 0
+    rows = np.zeros((B, Hq, len(tiles), BLOCK, D), np.float32)
+    for i, t in enumerate(tiles):
+        r1 = min(Sq, (t + 1) * BLOCK)
+        rows[:, :, i, :r1 - t * BLOCK] = out[:, :, t * BLOCK:r1]
+    return rows
+
+
+def router_from_cells(cells: np.ndarray, cfg: OracleConfig) -> dict:
+    """The router over per-(b, head, tile) margins (src/sparse_attention.py:708-718):
+    row grain -> head sum in head order, then / H (torch's mean), broadcast back;
+    quantile -> the k-th smallest of the expanded [B,H,Qt] values, NaN last
+    (kthvalue), k = max(1, int(q * numel)), trigger where value <= threshold;
+    abs -> value < fp32(tau)."""
+    cells = np.ascontiguousarray(cells, dtype=np.float32)
+    B, H, Qt = cells.shape
+    if cfg.router_grain == "row":
+        acc = cells[:, 0].copy()
+        for h in range(1, H):
+            acc = (acc + cells[:, h]).astype(np.float32)
+        eff = np.broadcast_to((acc / np.float32(H)).astype(np.float32)[:, None, :], (B, H, Qt)).copy()
+    else:
+        eff = cells.copy()
+    if cfg.router_mode == "quantile":
+        kq = max(1, int(float(cfg.router_quantile) * eff.size))
+        thresh = np.sort(eff.reshape(-1))[kq - 1]   # NaN sorts last
+        trig = eff <= thresh
+    else:
+        thresh = np.float32(cfg.router_tau)
+        trig = eff < thresh
+    return {"sigma_eff": eff, "thresh": np.float32(thresh), "trigger": trig}
 
 
 def canonical_sets(kv_idx: np.ndarray, S: int):

@@ -31,6 +31,7 @@
  */
 #include <float.h>
 #include <math.h>
+#include <omp.h>
 #include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
@@ -38,6 +39,11 @@
 #define BLK 64
 
 static inline int64_t cdiv64(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+/* Threads of the oracle's parallel regions (a process launched under torchrun
+ * inherits OMP_NUM_THREADS=1; the CPU baseline asks for every host core). */
+void oracle_set_threads(int n) { if (n > 0) omp_set_num_threads(n); }
+int oracle_get_threads(void) { return omp_get_max_threads(); }
 
 /* -------------------------------------------------------------------------- */
 /* Block summaries: sparse_attention.py:617-646                                */
@@ -89,73 +95,80 @@ int oracle_tile_scores_range(const float *Q, int64_t sb, int64_t sh, int64_t ss,
     if (t_begin < 0) t_begin = 0;
     if (t_end > Qt) t_end = Qt;
     const int G = Hq / Hkv;
-#pragma omp parallel for collapse(2) schedule(dynamic)
+    /* per (b, h): transposed summaries sT[d][blk] so the inner loop runs over
+     * blocks, then the tiles in parallel (each (row, block) chain is the same
+     * sequence of fmaf whichever thread runs it) */
+    float *sa = (float *)malloc(sizeof(float) * (size_t)D * NB);
+    float *sbT = quest ? (float *)malloc(sizeof(float) * (size_t)D * NB) : NULL;
     for (int b = 0; b < B; ++b)
         for (int h = 0; h < Hq; ++h) {
             const int kvh = h / G;
-            /* transposed summaries: sT[d][blk] so the inner loop runs over blocks */
-            float *sa = (float *)malloc(sizeof(float) * (size_t)D * NB);
-            float *sbT = quest ? (float *)malloc(sizeof(float) * (size_t)D * NB) : NULL;
-            float *acc = (float *)malloc(sizeof(float) * NB);
-            float *acc2 = (float *)malloc(sizeof(float) * NB);
-            float *qp = (float *)malloc(sizeof(float) * D);
-            float *qn = (float *)malloc(sizeof(float) * D);
             const float *A = summ_a + ((int64_t)b * Hkv + kvh) * NB * D;
             const float *Bm = quest ? summ_b + ((int64_t)b * Hkv + kvh) * NB * D : NULL;
+#pragma omp parallel for schedule(static)
             for (int nb = 0; nb < NB; ++nb)
                 for (int d = 0; d < D; ++d) {
                     sa[(size_t)d * NB + nb] = A[(int64_t)nb * D + d];
                     if (quest) sbT[(size_t)d * NB + nb] = Bm[(int64_t)nb * D + d];
                 }
-            for (int t = t_begin; t < t_end; ++t) {
-                float *row = ts + (((int64_t)b * Hq + h) * Qt + t) * NB;
-                int last = t * BLK + BLK - 1;
-                if (last > S - 1) last = S - 1;
-                const int nvis = last / BLK + 1;
-                for (int j = 0; j < NB; ++j) row[j] = -INFINITY;
-                for (int r = t * BLK; r < t * BLK + BLK; ++r) {
-                    if (r >= S) {
-                        /* zero-padded query row scores exactly 0 (F.pad, :623-625) */
-                        for (int j = 0; j < nvis; ++j) row[j] = (0.0f > row[j]) ? 0.0f : row[j];
-                        continue;
-                    }
-                    const float *q = Q + b * sb + h * sh + (int64_t)r * ss;
-                    for (int d = 0; d < D; ++d) {
-                        float x = q[d * sd];
-                        qp[d] = x > 0.0f ? x : 0.0f;
-                        qn[d] = x < 0.0f ? x : 0.0f;
-                    }
-                    for (int j = 0; j < nvis; ++j) { acc[j] = 0.0f; acc2[j] = 0.0f; }
-                    if (!quest) {
-                        for (int d = 0; d < D; ++d) {
-                            const float qd = q[d * sd];
-                            const float *col = sa + (size_t)d * NB;
-                            for (int j = 0; j < nvis; ++j) acc[j] = fmaf(qd, col[j], acc[j]);
+#pragma omp parallel
+            {
+                float *acc = (float *)malloc(sizeof(float) * NB);
+                float *acc2 = (float *)malloc(sizeof(float) * NB);
+                float *qp = (float *)malloc(sizeof(float) * D);
+                float *qn = (float *)malloc(sizeof(float) * D);
+#pragma omp for schedule(dynamic)
+                for (int t = t_begin; t < t_end; ++t) {
+                    float *row = ts + (((int64_t)b * Hq + h) * Qt + t) * NB;
+                    int last = t * BLK + BLK - 1;
+                    if (last > S - 1) last = S - 1;
+                    const int nvis = last / BLK + 1;
+                    for (int j = 0; j < NB; ++j) row[j] = -INFINITY;
+                    for (int r = t * BLK; r < t * BLK + BLK; ++r) {
+                        if (r >= S) {
+                            /* zero-padded query row scores exactly 0 (F.pad, :623-625) */
+                            for (int j = 0; j < nvis; ++j) row[j] = (0.0f > row[j]) ? 0.0f : row[j];
+                            continue;
                         }
-                        for (int j = 0; j < nvis; ++j) {
-                            float s = acc[j] * scale;
-                            row[j] = (s > row[j]) ? s : row[j];
-                        }
-                    } else {
-                        /* summ_a = Kmin, summ_b = Kmax */
+                        const float *q = Q + b * sb + h * sh + (int64_t)r * ss;
                         for (int d = 0; d < D; ++d) {
-                            const float *cmin = sa + (size_t)d * NB;
-                            const float *cmax = sbT + (size_t)d * NB;
-                            const float p = qp[d], n = qn[d];
-                            for (int j = 0; j < nvis; ++j) {
-                                acc[j] = fmaf(p, cmax[j], acc[j]);
-                                acc2[j] = fmaf(n, cmin[j], acc2[j]);
+                            float x = q[d * sd];
+                            qp[d] = x > 0.0f ? x : 0.0f;
+                            qn[d] = x < 0.0f ? x : 0.0f;
+                        }
+                        for (int j = 0; j < nvis; ++j) { acc[j] = 0.0f; acc2[j] = 0.0f; }
+                        if (!quest) {
+                            for (int d = 0; d < D; ++d) {
+                                const float qd = q[d * sd];
+                                const float *col = sa + (size_t)d * NB;
+                                for (int j = 0; j < nvis; ++j) acc[j] = fmaf(qd, col[j], acc[j]);
                             }
-                        }
-                        for (int j = 0; j < nvis; ++j) {
-                            float s = (acc[j] + acc2[j]) * scale;
-                            row[j] = (s > row[j]) ? s : row[j];
+                            for (int j = 0; j < nvis; ++j) {
+                                float s = acc[j] * scale;
+                                row[j] = (s > row[j]) ? s : row[j];
+                            }
+                        } else {
+                            /* summ_a = Kmin, summ_b = Kmax */
+                            for (int d = 0; d < D; ++d) {
+                                const float *cmin = sa + (size_t)d * NB;
+                                const float *cmax = sbT + (size_t)d * NB;
+                                const float p = qp[d], n = qn[d];
+                                for (int j = 0; j < nvis; ++j) {
+                                    acc[j] = fmaf(p, cmax[j], acc[j]);
+                                    acc2[j] = fmaf(n, cmin[j], acc2[j]);
+                                }
+                            }
+                            for (int j = 0; j < nvis; ++j) {
+                                float s = (acc[j] + acc2[j]) * scale;
+                                row[j] = (s > row[j]) ? s : row[j];
+                            }
                         }
                     }
                 }
+                free(acc); free(acc2); free(qp); free(qn);
             }
-            free(sa); free(sbT); free(acc); free(acc2); free(qp); free(qn);
         }
+    free(sa); free(sbT);
     return 0;
 }
 
@@ -384,54 +397,63 @@ int oracle_attn_range(const float *Q, int64_t qb, int64_t qh, int64_t qs, int64_
     const int G = Hq / Hkv;
     if (t_begin < 0) t_begin = 0;
     if (t_end > Qt) t_end = Qt;
-#pragma omp parallel for collapse(3) schedule(dynamic)
-    for (int b = 0; b < B; ++b)
-        for (int h = 0; h < Hq; ++h)
-            for (int t = t_begin; t < t_end; ++t) {
-                const int kvh = h / G;
-                const int32_t *slots = kv_idx + (((int64_t)b * Hq + h) * Qt + t) * kmax;
-                double *logit = (double *)malloc(sizeof(double) * (size_t)kmax * BLK);
-                int *keyn = (int *)malloc(sizeof(int) * (size_t)kmax * BLK);
-                double *acc = (double *)malloc(sizeof(double) * D);
-                const int tile_last = t * BLK + BLK - 1;
-                for (int m = t * BLK; m < t * BLK + BLK && m < Sq; ++m) {
-                    const float *q = Q + b * qb + h * qh + (int64_t)m * qs;
-                    int n_used = 0;
-                    double mx = -INFINITY;
-                    for (int j = 0; j < kmax; ++j) {
-                        const int blk = slots[j];
-                        if (blk < 0 || blk >= NB) continue;
-                        if (blk * BLK > tile_last) continue;
-                        for (int c = 0; c < BLK; ++c) {
-                            const int n = blk * BLK + c;
-                            if (n >= Sk || n > m) continue;
-                            const float *k = K + b * kb_ + kvh * kh + (int64_t)n * ks;
-                            double dot = 0.0;
-                            for (int d = 0; d < D; ++d) dot += (double)q[d * qd] * (double)k[d * kd];
-                            dot *= (double)scale;
-                            logit[n_used] = dot;
-                            keyn[n_used] = n;
-                            ++n_used;
-                            if (dot > mx) mx = dot;
-                        }
-                    }
-                    float *o = out + (((int64_t)b * Hq + h) * Sq + m) * D;
-                    if (n_used == 0) {
-                        for (int d = 0; d < D; ++d) o[d] = 0.0f;
-                        continue;
-                    }
-                    double l = 0.0;
-                    for (int d = 0; d < D; ++d) acc[d] = 0.0;
-                    for (int u = 0; u < n_used; ++u) {
-                        const double p = exp(logit[u] - mx);
-                        l += p;
-                        const float *v = V + b * vb + kvh * vh + (int64_t)keyn[u] * vs;
-                        for (int d = 0; d < D; ++d) acc[d] += p * (double)v[d * vd];
-                    }
-                    for (int d = 0; d < D; ++d) o[d] = (float)(acc[d] / l);
+    const int nt = t_end - t_begin;
+    if (nt <= 0) return 0;
+    /* one query row per iteration: (b, h, tile, row within the tile) */
+    const int64_t nrows = (int64_t)B * Hq * nt * BLK;
+#pragma omp parallel
+    {
+        double *logit = (double *)malloc(sizeof(double) * (size_t)kmax * BLK);
+        int *keyn = (int *)malloc(sizeof(int) * (size_t)kmax * BLK);
+        double *acc = (double *)malloc(sizeof(double) * D);
+#pragma omp for schedule(dynamic, 16)
+        for (int64_t it = 0; it < nrows; ++it) {
+            const int rr = (int)(it % BLK);
+            const int t = t_begin + (int)((it / BLK) % nt);
+            const int h = (int)((it / ((int64_t)BLK * nt)) % Hq);
+            const int b = (int)(it / ((int64_t)BLK * nt * Hq));
+            const int m = t * BLK + rr;
+            if (m >= Sq) continue;
+            const int kvh = h / G;
+            const int32_t *slots = kv_idx + (((int64_t)b * Hq + h) * Qt + t) * kmax;
+            const int tile_last = t * BLK + BLK - 1;
+            const float *q = Q + b * qb + h * qh + (int64_t)m * qs;
+            int n_used = 0;
+            double mx = -INFINITY;
+            for (int j = 0; j < kmax; ++j) {
+                const int blk = slots[j];
+                if (blk < 0 || blk >= NB) continue;
+                if (blk * BLK > tile_last) continue;
+                for (int c = 0; c < BLK; ++c) {
+                    const int n = blk * BLK + c;
+                    if (n >= Sk || n > m) continue;
+                    const float *k = K + b * kb_ + kvh * kh + (int64_t)n * ks;
+                    double dot = 0.0;
+                    for (int d = 0; d < D; ++d) dot += (double)q[d * qd] * (double)k[d * kd];
+                    dot *= (double)scale;
+                    logit[n_used] = dot;
+                    keyn[n_used] = n;
+                    ++n_used;
+                    if (dot > mx) mx = dot;
                 }
-                free(logit); free(keyn); free(acc);
             }
+            float *o = out + (((int64_t)b * Hq + h) * Sq + m) * D;
+            if (n_used == 0) {
+                for (int d = 0; d < D; ++d) o[d] = 0.0f;
+                continue;
+            }
+            double l = 0.0;
+            for (int d = 0; d < D; ++d) acc[d] = 0.0;
+            for (int u = 0; u < n_used; ++u) {
+                const double p = exp(logit[u] - mx);
+                l += p;
+                const float *v = V + b * vb + kvh * vh + (int64_t)keyn[u] * vs;
+                for (int d = 0; d < D; ++d) acc[d] += p * (double)v[d * vd];
+            }
+            for (int d = 0; d < D; ++d) o[d] = (float)(acc[d] / l);
+        }
+        free(logit); free(keyn); free(acc);
+    }
     return 0;
 }
 

@@ -20,6 +20,19 @@ seeded planted inputs (ugbsa.synth.planted_inputs), and records:
 Inputs are not stored: tests regenerate them from the recorded seed and shape
 and check ``input_digest`` first, so a generator change fails loudly.
 The fixtures are small (a few hundred KB in total).
+
+``--configs`` records the BASELINE configurations instead, into
+tests/golden/configs/ (``CONFIG_CASES``):
+
+* ``cfg1_layer``  config 1 in full (S=4096, 8/8 heads, d128, fp32, K-mean
+  router, k_base 8): kv_idx, tile scores, the per-head margins before the
+  row-grain mean (``cell_margin_ref``), the quantile, the ``SEL.log``
+  diagnostics (``kept_blocks_ref``, ``trigger_rate_ref``) and reference_attn
+  rows of a few (head, tile) samples;
+* ``cfg2_select`` config 2's selection (S=32768, 28/4 heads, d128, bf16 inputs
+  scored in fp32, Quest router, k_base 32, 16 chained planted blocks): the
+  canonical block sets as a packed bit mask, the per-head margins, the quantile
+  and the log diagnostics (its tile scores, 29 MB, are not stored).
 """
 from __future__ import annotations
 
@@ -82,6 +95,124 @@ CASES = {
         sel=dict(mode="router", router_score="mean", router_mode="quantile", router_grain="row",
                  router_quantile=0.25, budget_blocks=1, k_min=1, k_max=112), attn=True),
 }
+
+
+CONFIG_CASES = {
+    "cfg1_layer": dict(
+        inp=dict(B=1, Hq=8, Hkv=8, S=4096, D=128, n_planted=4, seed=0, chained=False, bf16=False),
+        sel=dict(mode="router", router_score="mean", router_mode="quantile", router_grain="row",
+                 router_quantile=0.25, budget_blocks=4, k_min=1, k_max=112),
+        store="full", attn_samples=[(0, 1), (0, 40), (3, 63), (7, 40), (7, 63)]),
+    "cfg2_select": dict(
+        inp=dict(B=1, Hq=28, Hkv=4, S=32768, D=128, n_planted=16, seed=2, chained=True, bf16=True),
+        sel=dict(mode="router", router_score="quest", router_mode="quantile", router_grain="row",
+                 router_quantile=0.25, budget_blocks=16, k_min=1, k_max=112),
+        store="sets", attn_samples=[]),
+}
+
+
+def pack_sets(kv_idx: np.ndarray, S: int) -> np.ndarray:
+    """Canonical sets (sentinel and causally invisible ids dropped) as a bit mask
+    [B, H, Qt, ceil(NB/8)] uint8 (np.packbits over the block axis)."""
+    nb = math.ceil(S / 64)
+    B, H, Qt, _ = kv_idx.shape
+    mask = np.zeros((B, H, Qt, nb), bool)
+    last_blk = np.minimum(np.arange(Qt) * 64 + 63, S - 1) // 64          # last visible block per tile
+    ids = kv_idx.astype(np.int64)
+    ok = (ids >= 0) & (ids < nb) & (ids <= last_blk[None, None, :, None])
+    b, h, t, j = np.nonzero(ok)
+    mask[b, h, t, ids[b, h, t, j]] = True
+    return np.packbits(mask, axis=-1)
+
+
+def run_reference_config(ref_src: str, name: str, spec: dict) -> dict:
+    """One BASELINE configuration through the reference's selector with SEL.log on."""
+    import torch
+
+    if ref_src not in sys.path:
+        sys.path.insert(0, ref_src)
+    import sparse_attention as sa
+    from transformers.models.qwen2.modeling_qwen2 import repeat_kv
+    from triton_block_attn import reference_attn
+
+    inp, sel = spec["inp"], spec["sel"]
+    q, k, v, planted = planted_inputs(inp["B"], inp["Hq"], inp["Hkv"], inp["S"], inp["D"],
+                                      n_planted=inp["n_planted"], seed=inp["seed"],
+                                      chained=inp["chained"], bf16=inp["bf16"])
+    S_, D = inp["S"], inp["D"]
+    scale = D ** -0.5
+    X = sa.SEL
+    X.kernel_v2 = True
+    for key in ("mode", "router_score", "router_mode", "router_grain", "router_quantile", "budget_blocks",
+                "k_min", "k_max"):
+        setattr(X, key, sel[key])
+    X.router_tau = sel.get("router_tau", 0.10)
+    X.log = True
+    X.reset_log()
+    g = inp["Hq"] // inp["Hkv"]
+    qt = torch.from_numpy(q)
+    kt = repeat_kv(torch.from_numpy(k), g)      # BASELINE's oracle: fp32 scores on repeat_kv'd keys
+    captured = {}
+    orig_topk, orig_kth, orig_mean = torch.Tensor.topk, torch.Tensor.kthvalue, torch.Tensor.mean
+
+    def topk_hook(self, *a, **kw):
+        if spec["store"] == "full":
+            captured["tile_score"] = self.detach().clone()
+        return orig_topk(self, *a, **kw)
+
+    def kth_hook(self, *a, **kw):
+        r = orig_kth(self, *a, **kw)
+        captured["margin"] = self.detach().clone()
+        captured["kquant"] = int(a[0] if a else kw["k"])
+        captured["thresh"] = float(r.values)
+        return r
+
+    def mean_hook(self, *a, **kw):
+        # the row-grain head mean of the per-tile margins (:708-710)
+        if (a[:1] == (1,) or kw.get("dim") == 1) and kw.get("keepdim") and self.dim() == 3:
+            captured["cell_margin"] = self.detach().clone()
+        return orig_mean(self, *a, **kw)
+
+    torch.Tensor.topk, torch.Tensor.kthvalue, torch.Tensor.mean = topk_hook, kth_hook, mean_hook
+    try:
+        kv = sa._block_select_kv_idx_v2(qt, kt, scale)
+    finally:
+        torch.Tensor.topk, torch.Tensor.kthvalue, torch.Tensor.mean = orig_topk, orig_kth, orig_mean
+    X.log = False
+    kv_np = kv.numpy().astype(np.int32)
+    out = {
+        "input_digest": input_digest(q, k, v),
+        "scale": np.float32(scale),
+        "meta": json.dumps({"name": name, "inp": inp, "sel": sel, "store": spec["store"],
+                            "attn_samples": spec["attn_samples"]}),
+        "kv_shape": np.array(kv_np.shape, np.int64),
+        "sets_ref": pack_sets(kv_np, S_),
+        "cell_margin_ref": captured["cell_margin"].numpy().astype(np.float32),
+        "margin_ref": captured["margin"].numpy().astype(np.float32),
+        "kquant_ref": np.int64(captured["kquant"]),
+        "thresh_ref": np.float32(captured["thresh"]),
+        "kept_blocks_ref": np.stack([x.numpy() for x in X.kept_blocks.values()]),
+        "trigger_rate_ref": np.array(X.router_trigger_rate, np.float64),
+        "budget_samples_ref": np.array(X.budget_samples, np.float64),
+    }
+    if spec["store"] == "full":
+        out["kv_idx_ref"] = kv_np
+        out["tile_score_ref"] = captured["tile_score"].numpy().astype(np.float32)
+    if spec["attn_samples"]:
+        vt = repeat_kv(torch.from_numpy(v), g)
+        nb = math.ceil(S_ / 64)
+        rows = []
+        for (h, t) in spec["attn_samples"]:
+            # reference_attn on one head with the tile-broadcast keep mask of that head
+            keep = torch.zeros(1, 1, S_, nb, dtype=torch.bool)
+            for tt in range(kv.shape[2]):
+                ids = kv[0, h, tt].long()
+                ids = ids[ids < nb]
+                keep[0, 0, tt * 64:min(S_, (tt + 1) * 64), ids] = True
+            o = reference_attn(qt[:, h:h + 1], kt[:, h:h + 1], vt[:, h:h + 1], keep, scale)
+            rows.append(o[0, 0, t * 64:min(S_, (t + 1) * 64)].numpy().astype(np.float32))
+        out["attn_rows_ref"] = np.stack(rows)
+    return out
 
 
 def run_reference(ref_src: str, name: str, spec: dict) -> dict:
@@ -172,8 +303,19 @@ def main():
     ap.add_argument("--ref", default=os.environ.get("UGBSA_REFERENCE"), required="UGBSA_REFERENCE" not in os.environ,
                     help="root of the reference project (its src/ is imported); or set UGBSA_REFERENCE")
     ap.add_argument("--only", default=None)
+    ap.add_argument("--configs", action="store_true", help="record the BASELINE configurations (CONFIG_CASES)")
     args = ap.parse_args()
     ref_src = os.path.join(args.ref, "src")
+    if args.configs:
+        os.makedirs(os.path.join(HERE, "configs"), exist_ok=True)
+        for name, spec in CONFIG_CASES.items():
+            if args.only and name != args.only:
+                continue
+            rec = run_reference_config(ref_src, name, spec)
+            path = os.path.join(HERE, "configs", f"{name}.npz")
+            np.savez_compressed(path, **rec)
+            print(f"wrote {path} ({os.path.getsize(path)} bytes)")
+        return
     for name, spec in CASES.items():
         if args.only and name != args.only:
             continue

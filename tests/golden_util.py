@@ -27,3 +27,41 @@ def load(name):
         raise AssertionError(f"{name}: regenerated inputs differ from the fixture's digest "
                              "(the synthetic generator changed)")
     return meta, (q, k, v), rec
+
+
+CONFIGS = os.path.join(GOLDEN, "configs")
+
+
+def load_config(name):
+    """A BASELINE-configuration fixture (tests/golden/configs/, make_golden.py
+    --configs): (meta, (q, k, v), record) with the inputs regenerated and checked."""
+    z = np.load(os.path.join(CONFIGS, name + ".npz"))
+    rec = {k: z[k] for k in z.files}
+    meta = json.loads(str(rec.pop("meta")))
+    inp = meta["inp"]
+    q, k, v, _ = planted_inputs(inp["B"], inp["Hq"], inp["Hkv"], inp["S"], inp["D"],
+                                n_planted=inp["n_planted"], seed=inp["seed"],
+                                chained=inp["chained"], bf16=inp["bf16"])
+    if input_digest(q, k, v) != str(rec["input_digest"]):
+        raise AssertionError(f"{name}: regenerated inputs differ from the fixture's digest")
+    return meta, (q, k, v), rec
+
+
+def unpack_sets(rec, S):
+    """The fixture's canonical sets as a bool mask [B, H, Qt, NB]."""
+    nb = (S + 63) // 64
+    return np.unpackbits(rec["sets_ref"], axis=-1, count=nb).astype(bool)
+
+
+def sets_mask(kv_idx, S):
+    """Canonical sets of a kv_idx array (sentinel and causally invisible ids
+    dropped) as a bool mask [B, H, Qt, NB]."""
+    nb = (S + 63) // 64
+    B, H, Qt, _ = kv_idx.shape
+    last_blk = np.minimum(np.arange(Qt) * 64 + 63, S - 1) // 64
+    ids = kv_idx.astype(np.int64)
+    ok = (ids >= 0) & (ids < nb) & (ids <= last_blk[None, None, :, None])
+    mask = np.zeros((B, H, Qt, nb), bool)
+    b, h, t, j = np.nonzero(ok)
+    mask[b, h, t, ids[b, h, t, j]] = True
+    return mask

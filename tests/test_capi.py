@@ -87,9 +87,12 @@ def test_argument_validation_without_device():
     # workspace too small
     assert L.ugbsa_select(fake, _lib.BF16, st, fake, None, 1, 8, 8, 4096, 128, ctypes.c_float(0.1),
                           ctypes.byref(c), fake, 64, None, None, fake, 8, None) == 6
-    # attention: fp32 is not a tensor-core input here, head_dim 96 unsupported
-    assert L.ugbsa_attn(fake, fake, fake, _lib.F32, st, st, st, fake, 16, 1, 8, 8, 4096, 4096, 128,
+    # attention: an unknown dtype; fp32 (the CUDA-core kernel) has no output peers; head_dim 96 unsupported
+    assert L.ugbsa_attn(fake, fake, fake, 7, st, st, st, fake, 16, 1, 8, 8, 4096, 4096, 128,
                         ctypes.c_float(0.1), fake, st, None) == 3
+    peers = (ctypes.c_void_p * 1)(fake)
+    assert L.ugbsa_attn_rows_peers(fake, fake, fake, _lib.F32, st, st, st, fake, 16, 1, 8, 8, 4096, 4096, 128, 0,
+                                   1, ctypes.c_float(0.1), fake, st, peers, 1, None) == 3
     assert L.ugbsa_attn(fake, fake, fake, _lib.BF16, st, st, st, fake, 16, 1, 8, 8, 4096, 4096, 96,
                         ctypes.c_float(0.1), fake, st, None) == 5
     # arithmetic check: negative count, null operand
@@ -241,6 +244,17 @@ def test_workspace_sizes():
     assert L.ugbsa_select_workspace_bytes(ctypes.byref(c), 1, 28, 131072) >= 28 * 2048 * 4
     assert L.ugbsa_select_finish_workspace_bytes(1, 131072) >= 2048 * 4
     assert L.ugbsa_select_workspace_bytes(ctypes.byref(c), 0, 28, 131072) == 0
+    # the exact size depends on dtype, head dim and KV heads; the dtype-free query bounds all of them
+    for dt in (_lib.F32, _lib.BF16, _lib.F16):
+        for D in (64, 128, 256):
+            for Hkv in (1, 4, 28):
+                ex = L.ugbsa_select_workspace_bytes_ex(ctypes.byref(c), dt, 1, 28, Hkv, 8192, D)
+                assert 0 < ex <= L.ugbsa_select_workspace_bytes(ctypes.byref(c), 1, 28, 8192)
+    # bf16 head dim 256 with Hkv = Hq needs more than head dim 128 with Hkv = Hq
+    e256 = L.ugbsa_select_workspace_bytes_ex(ctypes.byref(c), _lib.BF16, 1, 4, 4, 2048, 256)
+    e128 = L.ugbsa_select_workspace_bytes_ex(ctypes.byref(c), _lib.BF16, 1, 4, 4, 2048, 128)
+    assert e256 > e128
+    assert L.ugbsa_select_workspace_bytes_ex(ctypes.byref(c), _lib.BF16, 1, 4, 0, 2048, 128) == 0
 
 
 def test_ops_refuse_cpu_tensors():

@@ -134,6 +134,51 @@ def _check_select(case):
     assert np.array_equal(trig.cpu().numpy(), want["trigger"])
 
 
+@pytest.mark.parametrize("score", ["mean", "quest"])
+def test_select_exact_workspace_guarded_d256_mha(score):
+    """bf16 at head dim 256 with as many KV heads as query heads (the largest
+    operand copies per query head): ugbsa_select gets exactly the bytes
+    ugbsa_select_workspace_bytes_ex reports, followed by a 4 KB guard filled
+    with a pattern.  The guard must be untouched and kv_idx / sigma bit-exact
+    against the oracle; 256 bytes fewer is refused with UGBSA_ERR_WORKSPACE, and
+    the dtype-free size query is at least the exact size."""
+    import ctypes
+    from ugbsa import _lib
+    B, Hq, Hkv, S, D = 1, 4, 4, 2048, 256
+    q, k, _, _ = planted_inputs(B, Hq, Hkv, S, D, n_planted=4, seed=91, bf16=True)
+    ocfg, gcfg = _cfgs("router", score=score, budget=4)
+    qd, kd = _dev(q, torch.bfloat16), _dev(k, torch.bfloat16)
+    summ = ops.block_summary(kd, gcfg.quest)
+    sa_, sb_ = summ if gcfg.quest else (summ, None)
+    _, kmax = ops.budget(gcfg, S)
+    Qt = S // 64
+    kv = torch.empty((B, Hq, Qt, kmax), device=DEV, dtype=torch.int32)
+    sigma = torch.empty((B, Hq, Qt), device=DEV, dtype=torch.float32)
+    trig = torch.empty((B, Hq, Qt), device=DEV, dtype=torch.uint8)
+    c = gcfg.to_c()
+    L = _lib.load()
+    nbytes = L.ugbsa_select_workspace_bytes_ex(ctypes.byref(c), _lib.BF16, B, Hq, Hkv, S, D)
+    assert L.ugbsa_select_workspace_bytes(ctypes.byref(c), B, Hq, S) >= nbytes
+    guard = 4096
+    ws = torch.full((nbytes + guard,), 0xA5, device=DEV, dtype=torch.uint8)
+    p_ = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else None
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    call = lambda n: L.ugbsa_select(p_(qd), _lib.BF16, _lib.Strides(*qd.stride()), p_(sa_), p_(sb_), B, Hq, Hkv, S,
+                                    D, ctypes.c_float(D ** -0.5), ctypes.byref(c), p_(kv), kmax, p_(sigma),
+                                    p_(trig), p_(ws), ctypes.c_size_t(n), stream)
+    assert call(nbytes - 256) == 6   # UGBSA_ERR_WORKSPACE
+    assert call(nbytes) == 0
+    torch.cuda.synchronize()
+    assert bool((ws[nbytes:] == 0xA5).all()), "selection wrote past the workspace it was given"
+    want = oracle.select(q, k, D ** -0.5, ocfg)
+    assert np.array_equal(kv.cpu().numpy(), want["kv_idx"])
+    s_got, s_want = sigma.cpu().numpy(), want["sigma_eff"]
+    nan = np.isnan(s_want)
+    assert np.array_equal(nan, np.isnan(s_got))
+    assert np.array_equal(s_got[~nan].view(np.uint32), s_want[~nan].view(np.uint32))
+    assert np.array_equal(trig.cpu().numpy(), want["trigger"])
+
+
 @pytest.mark.parametrize("passes", ["two", "one"])
 @pytest.mark.parametrize("score", ["quest", "mean"])
 def test_tensor_core_guided_tile_scores_exact(score, passes, monkeypatch):

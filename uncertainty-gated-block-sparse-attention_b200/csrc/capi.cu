@@ -126,6 +126,13 @@ size_t ugbsa_select_workspace_bytes(const ugbsa_selector_config *cfg, int B, int
     return select_workspace_bytes(B, Hq, S);
 }
 
+size_t ugbsa_select_workspace_bytes_ex(const ugbsa_selector_config *cfg, int dtype, int B, int Hq, int Hkv, int S,
+                                       int D) {
+    (void)cfg;
+    if (B <= 0 || Hq <= 0 || Hkv <= 0 || S <= 0 || D <= 0) return 0;
+    return select_workspace_bytes_exact(dtype, B, Hq, Hkv, S, D);
+}
+
 int ugbsa_block_summary(const void *K, int dtype, ugbsa_strides ks, int B, int Hkv, int S, int D, int quest,
                         float *out_a, float *out_b, float *out_norm, ugbsa_stream_t stream) {
     if (B <= 0 || Hkv <= 0 || S <= 0 || D <= 0) return UGBSA_ERR_SHAPE;
@@ -157,7 +164,8 @@ int ugbsa_select(const void *Q, int dtype, ugbsa_strides qs, const float *summ_a
     int kb, km;
     budget(cfg, NB, &kb, &km);
     if (km != kmax) return UGBSA_ERR_SHAPE;
-    if (!workspace || workspace_bytes < select_workspace_bytes(B, Hq, S)) return UGBSA_ERR_WORKSPACE;
+    if (!workspace || workspace_bytes < select_workspace_bytes_exact(dtype, B, Hq, Hkv, S, D))
+        return UGBSA_ERR_WORKSPACE;
     if (!aligned16(workspace)) return UGBSA_ERR_ALIGN;
     return launch_select(Q, dtype, qs, summ_a, summ_b, B, Hq, Hkv, S, D, scale, cfg, kb, km, kv_idx, sigma,
                          trigger, workspace, reinterpret_cast<cudaStream_t>(stream));
@@ -254,12 +262,20 @@ static int attn_checked(const void *Q, const void *K, const void *V, int dtype, 
     int rc;
     if ((row_base != 0 || pair_stride != 1) && (rc = check_tiles(Sk, row_base, pair_stride, Sq, 64))) return rc;
     if (D != 64 && D != 128 && D != 256) return UGBSA_ERR_UNSUPPORTED;
-    if (dtype != UGBSA_BF16 && dtype != UGBSA_F16) return UGBSA_ERR_DTYPE;
+    if (dtype != UGBSA_BF16 && dtype != UGBSA_F16 && dtype != UGBSA_F32) return UGBSA_ERR_DTYPE;
     if ((rc = check_view(Q, dtype, qs)) || (rc = check_view(K, dtype, ks)) || (rc = check_view(V, dtype, vs)) ||
         (rc = check_view(out, dtype, os)))
         return rc;
     if (!kv_idx) return UGBSA_ERR_ARG;
     if (npeers < 0 || npeers > UGBSA_MAX_PEERS || (npeers > 0 && !peers)) return UGBSA_ERR_ARG;
+    if (dtype == UGBSA_F32) {   // CUDA-core kernel; output peers are a bf16 / fp16 feature
+        if (npeers > 0) return UGBSA_ERR_DTYPE;
+        if (kmax > 8192) return UGBSA_ERR_SHAPE;
+        return launch_attn_f32(static_cast<const float *>(Q), static_cast<const float *>(K),
+                               static_cast<const float *>(V), qs, ks, vs, kv_idx, kmax, B, Hq, Hkv, Sq, Sk, D,
+                               row_base / 64, pair_stride, scale, static_cast<float *>(out), os,
+                               reinterpret_cast<cudaStream_t>(stream));
+    }
     for (int i = 0; i < npeers; ++i)
         if ((rc = check_view(peers[i], dtype, os))) return rc;
     if (kmax > 8192) return UGBSA_ERR_SHAPE;

@@ -535,17 +535,29 @@ __global__ void __launch_bounds__(256) select_finalize_kernel(const FinParams p)
 static int64_t al256(int64_t x) { return (x + 255) / 256 * 256; }
 
 // workspace: [tensor-core scoring scratch][sigma cells][row sums][row means][thresh]
-// The scratch term is an upper bound (Hkv <= Hq, head_dim <= 128 on that path).
-size_t select_workspace_bytes(int B, int Hq, int S) {
+static size_t select_tail_bytes(int B, int Hq, int S) {
     const int64_t Qt = (S + 63) / 64;
     const int64_t cells = (int64_t)B * Hq * Qt;
     const int64_t rows = (int64_t)B * Qt;
-    return al256((int64_t)tc_scratch_bytes(B, Hq, Hq, S, 128, (int)Qt)) + (size_t)(al256(cells * 4) + 2 * al256(rows * 4) + 256);
+    return (size_t)(al256(cells * 4) + 2 * al256(rows * 4) + 256);
+}
+
+// Bound over every dtype, head dim (<= 256) and KV head count (<= Hq): the
+// tensor-core scratch is largest at D = 256 with Hkv = Hq.
+size_t select_workspace_bytes(int B, int Hq, int S) {
+    const int Qt = (S + 63) / 64;
+    return al256((int64_t)tc_scratch_bytes(B, Hq, Hq, S, 256, Qt)) + select_tail_bytes(B, Hq, S);
 }
 
 // what the tiles stage reads from the front of the workspace
 size_t select_tiles_scratch_bytes(int dtype, int B, int Hq, int Hkv, int S, int D, int Qt) {
     return tc_select_supported(dtype, D) ? al256((int64_t)tc_scratch_bytes(B, Hq, Hkv, S, D, Qt)) : 0;
+}
+
+// exactly what launch_select lays out for this problem
+size_t select_workspace_bytes_exact(int dtype, int B, int Hq, int Hkv, int S, int D) {
+    const int Qt = (S + 63) / 64;
+    return select_tiles_scratch_bytes(dtype, B, Hq, Hkv, S, D, Qt) + select_tail_bytes(B, Hq, S);
 }
 
 size_t select_finish_workspace_bytes(int B, int S) {

@@ -13,8 +13,14 @@
 // Properties of that array:
 //  * file-scope, statically sized at UGBSA_NOALLOC_SCRATCH_BYTES (1 MiB): every
 //    GPU that loads libugbsa holds these bytes until the process exits;
-//  * problems whose scratch would exceed it are rejected with
-//    UGBSA_ERR_TOO_LARGE (about 250K tiles x heads, e.g. 28 heads at 512K tokens);
+//  * a call is accepted when the scratch ugbsa_select would lay out for it,
+//    ugbsa_select_workspace_bytes_ex(cfg, dtype, B, Hq, Hkv, S, D), fits in it,
+//    and refused with UGBSA_ERR_TOO_LARGE otherwise.  With bf16 Q and head_dim
+//    64, 128 or 256 (the tensor-core scorer) that scratch holds the exact tile
+//    scores, 4 * B * Hq * ceil(S/64)^2 bytes, which grows with the square of the
+//    sequence: 28 query / 4 KV heads at head_dim 128 fit up to about 5K tokens,
+//    one head up to about 28K.  Other dtypes and head dims need only about
+//    4 * B * (Hq + 2) * ceil(S/64) bytes (28 heads: any S the selector accepts);
 //  * shared by every call on a device and never cleared: each call writes every
 //    scratch element it later reads, so nothing has to start at zero, but two
 //    calls whose kernels overlap on the GPU (different streams, no ordering)
@@ -58,8 +64,8 @@ extern "C" int ugbsa_select_noalloc(const void *Q, int dtype, ugbsa_strides qs, 
                                     const float *summ_b, int B, int Hq, int Hkv, int S, int D, float scale,
                                     const ugbsa_selector_config *cfg, int32_t *kv_idx, int kmax, float *sigma,
                                     uint8_t *trigger, ugbsa_stream_t stream) {
-    if (B <= 0 || Hq <= 0 || S <= 0) return UGBSA_ERR_SHAPE;
-    const size_t need = ugbsa::select_workspace_bytes(B, Hq, S);
+    if (B <= 0 || Hq <= 0 || Hkv <= 0 || S <= 0 || D <= 0) return UGBSA_ERR_SHAPE;
+    const size_t need = ugbsa::select_workspace_bytes_exact(dtype, B, Hq, Hkv, S, D);
     if (need > UGBSA_NOALLOC_SCRATCH_BYTES) return UGBSA_ERR_TOO_LARGE;
     void *scratch = nullptr;
     const int rc = scratch_address(&scratch);

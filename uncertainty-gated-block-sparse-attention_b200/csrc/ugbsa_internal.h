@@ -19,7 +19,10 @@ int launch_block_summary(const void *K, int dtype, ugbsa_strides ks, int B, int 
 int launch_block_summary_range(const void *K, int dtype, ugbsa_strides ks, int B, int Hkv, int S, int D, int quest,
                                int nb0, int NBo, float *out_a, float *out_b, float *out_norm, cudaStream_t stream);
 
+// bound over dtype, head dim and KV heads (the legacy size query)
 size_t select_workspace_bytes(int B, int Hq, int S);
+// what launch_select lays out (ugbsa_select checks against this)
+size_t select_workspace_bytes_exact(int dtype, int B, int Hq, int Hkv, int S, int D);
 size_t select_finish_workspace_bytes(int B, int S);
 // Qt: the tiles the call scores (all ceil(S/64) unless the query rows are a slice)
 size_t select_tiles_scratch_bytes(int dtype, int B, int Hq, int Hkv, int S, int D, int Qt);
@@ -95,6 +98,10 @@ int launch_attn(const void *Q, const void *K, const void *V, int dtype, ugbsa_st
                 ugbsa_strides vs, const int32_t *kv_idx, int kmax, int B, int Hq, int Hkv, int Sq, int Sk, int D,
                 int t_base, int pair_stride, float scale, void *out, ugbsa_strides os, void *const *peers,
                 int npeers, cudaStream_t stream, int *err);
+// fp32 Q/K/V (CUDA cores, attn_f32.cu); same row mapping as launch_attn, no peers
+int launch_attn_f32(const float *Q, const float *K, const float *V, ugbsa_strides qs, ugbsa_strides ks,
+                    ugbsa_strides vs, const int32_t *kv_idx, int kmax, int B, int Hq, int Hkv, int Sq, int Sk, int D,
+                    int t_base, int pair_stride, float scale, float *out, ugbsa_strides os, cudaStream_t stream);
 // two-tile (M=128) variant for D = 64 / 128; UGBSA_ERR_UNSUPPORTED when its
 // shared memory does not fit (the caller then uses launch_attn's single-tile kernel)
 int launch_attn_pair(const void *Q, const void *K, const void *V, int dtype, ugbsa_strides qs, ugbsa_strides ks,

@@ -49,6 +49,7 @@ SIGNATURES = {
     "ugbsa_status_string": (ctypes.c_char_p, [I]),
     "ugbsa_select_budget": (I, [ctypes.POINTER(SelectorConfig), I, ctypes.POINTER(I), ctypes.POINTER(I)]),
     "ugbsa_select_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(SelectorConfig), I, I, I]),
+    "ugbsa_select_workspace_bytes_ex": (ctypes.c_size_t, [ctypes.POINTER(SelectorConfig), I, I, I, I, I, I]),
     "ugbsa_block_summary": (I, [P, I, Strides, I, I, I, I, I, P, P, P, P]),
     "ugbsa_select": (I, [P, I, Strides, P, P, I, I, I, I, I, ctypes.c_float, ctypes.POINTER(SelectorConfig),
                          P, I, P, P, P, ctypes.c_size_t, P]),

@@ -124,7 +124,8 @@ def select_kv_idx(query: torch.Tensor, key: torch.Tensor, scaling: float, cfg: S
     Qt = math.ceil(S / BLOCK)
     kv_idx = torch.empty((B, Hq, Qt, kmax), device=query.device, dtype=torch.int32)
     c = cfg.to_c()
-    ws_bytes = _lib.load().ugbsa_select_workspace_bytes(ctypes.byref(c), B, Hq, S)
+    ws_bytes = _lib.load().ugbsa_select_workspace_bytes_ex(ctypes.byref(c), _DTYPES[query.dtype], B, Hq,
+                                                           key.shape[1], S, D)
     ws = torch.empty((ws_bytes,), device=query.device, dtype=torch.uint8)
     sigma = torch.empty((B, Hq, Qt), device=query.device, dtype=torch.float32) if return_router else None
     trig = torch.empty((B, Hq, Qt), device=query.device, dtype=torch.uint8) if return_router else None
@@ -153,8 +154,10 @@ def block_sparse_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kv_idx:
     (ugbsa_attn_rows_peers).
     """
     _need_cuda(q, k, v, kv_idx)
-    if q.dtype not in (torch.bfloat16, torch.float16) or k.dtype != q.dtype or v.dtype != q.dtype:
-        raise ValueError("block_sparse_attn takes bf16 or fp16 q/k/v of one dtype")
+    if q.dtype not in (torch.bfloat16, torch.float16, torch.float32) or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise ValueError("block_sparse_attn takes bf16, fp16 or fp32 q/k/v of one dtype")
+    if peer_out and q.dtype == torch.float32:
+        raise ValueError("output peers take bf16 / fp16 outputs")
     if kv_idx.dtype != torch.int32:
         raise ValueError("kv_idx must be int32")
     B, Hq, Sq, D = q.shape
@@ -383,7 +386,7 @@ def select_tiles(query: torch.Tensor, summ, n_kv_heads: int, scaling: float, cfg
     rowsum = torch.empty((B, Qt), device=query.device, dtype=torch.float32) if want_rowsum else None
     c = cfg.to_c()
     L = _lib.load()
-    ws_bytes = L.ugbsa_select_workspace_bytes(ctypes.byref(c), B, Hq, S)
+    ws_bytes = L.ugbsa_select_workspace_bytes_ex(ctypes.byref(c), _DTYPES[query.dtype], B, Hq, n_kv_heads, S, D)
     ws = torch.empty((ws_bytes,), device=query.device, dtype=torch.uint8)
     if row_base or Sq != S or pair_stride != 1:
         rc = L.ugbsa_select_tiles_rows(_ptr(query), _DTYPES[query.dtype], _strides(query), _ptr(sa), _ptr(sb), B,

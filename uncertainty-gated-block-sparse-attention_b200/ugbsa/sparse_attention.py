@@ -58,9 +58,15 @@ class Selector:
         self.reset_log()
 
     def reset_log(self):
+        # filled by the v2 selector while ``log`` is set, as the reference does
+        # (src/sparse_attention.py:726-744): per call, the blocks the last query
+        # tile keeps unioned over heads (bool [n_blocks] on the host, keyed by
+        # call order), the slot count, and the router's trigger fraction
         self.kept_blocks = {}
         self.budget_samples = []
         self.router_trigger_rate = []
+        self.router_eff_budget = []
+        self.router_margin_mean = []
 
     def config(self) -> ops.SelectorConfig:
         """Frozen snapshot of the knobs, as handed to the C ABI."""
@@ -122,13 +128,25 @@ def _block_select_kv_idx_v2(query, key_states, scaling, block_m=64):
     if block_m != BLOCK:
         raise ValueError("block_m is fixed at 64")
     cfg = SEL.config()
-    if SEL.log and cfg.mode == "router":
+    if not SEL.log:
+        return ops.select_kv_idx(query, key_states, float(scaling), cfg)
+    S = query.shape[-2]
+    k_base, kmax = ops.budget(cfg, S)
+    n_blocks = math.ceil(key_states.shape[-2] / BLOCK)
+    if cfg.mode == "router" and k_base < kmax:
         kv_idx, sigma, trig = ops.select_kv_idx(query, key_states, float(scaling), cfg, return_router=True)
-        SEL.router_trigger_rate.append(trig.float().mean())  # stays on device (no host sync)
+        # a host float per call, as the reference appends (:726-728; a sync only while logging)
+        SEL.router_trigger_rate.append(float(trig.float().mean().item()))
     else:
         kv_idx = ops.select_kv_idx(query, key_states, float(scaling), cfg)
-    if SEL.log:
-        SEL.budget_samples.append(float(kv_idx.shape[-1]))
+    # the last query tile's kept blocks of batch 0, unioned over heads, sentinels
+    # dropped (:733-743); read by the reference's needle-hit metric
+    last = kv_idx[0, :, -1, :].long().flatten()
+    last = last[last < n_blocks]
+    kept = torch.zeros(n_blocks, dtype=torch.bool, device=kv_idx.device)
+    kept.scatter_(0, last, True)
+    SEL.kept_blocks[len(SEL.kept_blocks)] = kept.cpu()
+    SEL.budget_samples.append(float(kmax))
     return kv_idx
 
 
