@@ -7,22 +7,28 @@ ratio vs dense on same GPU"): one attention layer of the Qwen2.5-7B geometry at
 block 64, router-on-Quest scoring, k_base = NB/16 = 128 slots per tile, q=0.25
 quantile router (triggered tiles keep 256), causal.  Inputs are seeded
 synthetic N(0,1) tensors with 16 chained planted key blocks per KV head.
+``--workload cfg5`` measures BASELINE config 5 instead (head_dim 256, 16 Q / 2
+KV heads, RMSNorm + RoPE on Q and K, 32 planted blocks, K-mean router, k_base
+128).
 
 A step is one pass of the hot path over that layer: block summaries, tile
-scoring + top-k + sigma router + kv_idx (3 launches), block-sparse attention
-(1 launch).  ``value`` is effective TFLOP/s = dense-equivalent block-causal
-FLOPs of the layer / step time, with inputs resident in HBM; ``e2e`` is the
-same metric through the public hook ``ugbsa.sparse_attention.block_sparse_attention``
-with Q/K/V copied from pinned host memory and the output copied back every step.
+scoring + top-k + sigma router + kv_idx, block-sparse attention.  ``value`` is
+effective TFLOP/s = dense-equivalent block-causal FLOPs of the layer / step
+time, with inputs resident in HBM; ``e2e`` is the same metric through the
+public hook ``ugbsa.sparse_attention.block_sparse_attention`` with Q/K/V copied
+from pinned host memory and the output copied back every step.
 
-Multi-GPU (torchrun, one rank per GPU): the layer's heads are sharded over the
-ranks (ugbsa.parallel): KV-head groups when they divide, Q heads within groups
-otherwise; one NCCL all-reduce of per-tile sigma sums feeds the shared quantile
-and one all-gather assembles the output.  Total work is fixed: "scaling": "strong".
+Multi-GPU (torchrun, one rank per GPU): KV-head groups are split over the
+ranks, and when the ranks outnumber the KV heads, each group's query-tile pairs
+are dealt round-robin over its ranks (ugbsa.parallel.GridShardedPrefill).  One
+NCCL all-reduce of per-tile sigma sums feeds the shared quantile; the attention
+kernel writes each output tile to every rank's buffer over NVLink (peer
+stores), and one small all-reduce orders the step's end.  Total work is fixed:
+"scaling": "strong".
 
 ``--impl reference`` times the CPU restatement of the reference path (the
-reference itself is Python/PyTorch and cannot be built as a library) on this
-host's cores, on a bounded sample of the same workload.
+reference itself is Python/PyTorch, absent from the GPU box) on every host
+core, on a bounded sample of the same workload.
 """
 from __future__ import annotations
 
@@ -50,14 +56,27 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # dram__bytes_write.sum): the 64K capture summarised in profiles/ (680.0 + 450.5 MB =
 # 1.131 GB, 1.05x its algorithmic bytes) scaled by 2, every term of which is linear in S at
 # fixed heads
-ATTN_TRAFFIC_BYTES = {131072: 2 * 1130506496, 65536: 1130506496}
+ATTN_TRAFFIC_BYTES = {("attn-layer", 131072): 2 * 1130506496, ("attn-layer", 65536): 1130506496}
+
+
+# --workload: "attn-layer" (the metric's layer, Qwen2.5-7B geometry, router-on-Quest) or
+# "cfg5" (head_dim 256, 16 Q / 2 KV heads, per-head RMSNorm + RoPE on
+# Q and K, 32 planted blocks, K-mean router with k_base 128 at 128K)
+WORKLOAD = "attn-layer"
 
 
 def workload(seq):
-    return dict(B=1, Hq=28, Hkv=4, S=seq, D=128, n_planted=16, seed=0,
+    nb = seq // 64
+    if WORKLOAD == "cfg5":
+        return dict(name="cfg5", B=1, Hq=16, Hkv=2, S=seq, D=256, n_planted=32, seed=5, chained=False,
+                    qk_norm_rope=True,
+                    sel=dict(mode="router", router_score="mean", router_mode="quantile", router_grain="row",
+                             router_quantile=0.25, budget_blocks=max(1, nb // 32), k_min=1,
+                             k_max=max(112, nb // 32)))
+    return dict(name="attn-layer", B=1, Hq=28, Hkv=4, S=seq, D=128, n_planted=16, seed=0, chained=True,
+                qk_norm_rope=False,
                 sel=dict(mode="router", router_score="quest", router_mode="quantile", router_grain="row",
-                         router_quantile=0.25, budget_blocks=max(1, (seq // 64) // 32), k_min=1,
-                         k_max=max(112, (seq // 64) // 32)))
+                         router_quantile=0.25, budget_blocks=max(1, nb // 32), k_min=1, k_max=max(112, nb // 32)))
 
 
 def split_for(world, requested="auto"):
@@ -92,9 +111,11 @@ def config_for(seq, world, split="auto"):
     gb = lambda n: f"{n / 1e6:.0f} MB"
     q_bytes = w["B"] * w["Hq"] * seq * w["D"] * 2
     kv_bytes = w["B"] * w["Hkv"] * seq * w["D"] * 2
-    return {"workload": f"attn-layer-{seq // 1024}K: B={w['B']} S={seq} Hq={w['Hq']} Hkv={w['Hkv']} D={w['D']} bf16 "
-                        f"block=64 router-on-Quest quantile row-grain q={s['router_quantile']} k_base={k_base} "
-                        f"kmax={kmax} causal",
+    score = "router-on-Quest" if s["router_score"] == "quest" else "K-mean router"
+    extra = " inputs: per-head RMSNorm + RoPE on Q and K" if w["qk_norm_rope"] else ""
+    return {"workload": f"{w['name']}-{seq // 1024}K: B={w['B']} S={seq} Hq={w['Hq']} Hkv={w['Hkv']} D={w['D']} "
+                        f"bf16 block=64 {score} quantile row-grain q={s['router_quantile']} k_base={k_base} "
+                        f"kmax={kmax} causal{extra}",
             "global_batch": w["B"], "seq_len": seq,
             "parallelism": parallelism_name(seq, world, split) if world > 1 else "none",
             "l2": f"inputs larger than L2 (Q {gb(q_bytes)}, K {gb(kv_bytes)}, V {gb(kv_bytes)})"}
@@ -267,8 +288,8 @@ def run_gpu(args, seq):
     sa.SEL.router_quantile, sa.SEL.budget_blocks = s["router_quantile"], s["budget_blocks"]
     sa.SEL.k_min, sa.SEL.k_max = s["k_min"], s["k_max"]
 
-    q, k, v = planted_inputs_torch(B, Hq, Hkv, S, D, n_planted=w["n_planted"], seed=w["seed"], chained=True,
-                                   dtype=torch.bfloat16, device=dev)
+    q, k, v = planted_inputs_torch(B, Hq, Hkv, S, D, n_planted=w["n_planted"], seed=w["seed"], chained=w["chained"],
+                                   qk_norm_rope=w["qk_norm_rope"], dtype=torch.bfloat16, device=dev)
     split = split_for(world, args.split)
     t0, pstride = 0, 1
     if world > 1 and split == "grid":
@@ -399,7 +420,8 @@ def run_gpu(args, seq):
     line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded N(0,1) + 16 chained planted blocks per KV head)",
+            "data": (f"synthetic (seeded N(0,1) + {w['n_planted']} {'chained ' if w['chained'] else ''}planted blocks "
+                     f"per KV head{', RMSNorm + RoPE applied' if w['qk_norm_rope'] else ''})"),
             "config": config_for(seq, world, split),
             "sparse_ms_per_layer": round(ms_per_step, 3),
             "select_ms": round(sel_sum / args.steps, 3), "attn_ms": round(attn_ms_avg, 3),
@@ -408,7 +430,7 @@ def run_gpu(args, seq):
             "roofline": {"bound": "tensor", "kernel": "attn_fwd_kernel", "achieved": round(achieved, 2),
                          "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
                          "peak_kind": f"bf16_tflops_sustained ({peak_kind})",
-                         "traffic": ATTN_TRAFFIC_BYTES.get(seq) if world == 1 else None},
+                         "traffic": ATTN_TRAFFIC_BYTES.get((w["name"], seq)) if world == 1 else None},
             "gpu_launches": parallel.launches_per_step(cfg, *ops.budget(cfg, S)) * args.steps,
             "clocks": clocks, "e2e": e2e, "cpu_baseline": cpu}
     if dense is not None:
@@ -419,6 +441,143 @@ def run_gpu(args, seq):
         line["stages"] = stages
     if per_rank is not None:
         line["per_rank_ms"] = per_rank
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------- full-model prefill
+def run_model(args):
+    """BASELINE configs 3 / 4: a whole prefill of a random-init Qwen2.5-7B (cfg3) or
+    14B (cfg4) shaped decoder, tensor-parallel over the ranks (ugbsa.decoder), with
+    the block-sparse attention on every layer, beside the same model with dense
+    SDPA attention.  A step is one forward over S uniform random token ids."""
+    import torch
+    import torch.distributed as dist
+
+    from ugbsa import decoder, ops
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+    shape = decoder.QWEN25_7B if args.workload == "cfg3" else decoder.QWEN25_14B
+    S = args.seq
+    nb = math.ceil(S / 64)
+    if args.workload == "cfg3":   # router-on-Quest, k_base = NB/16, q = 0.25
+        sel = dict(mode="router", router_score="quest", router_mode="quantile", router_grain="row",
+                   router_quantile=0.25, budget_blocks=max(1, nb // 32), k_min=1, k_max=max(112, nb // 32))
+        policy = "router-on-Quest"
+    else:                         # top-k 32 blocks: router-on-Quest, Quest or K-mean top-k
+        m = args.policy
+        sel = dict(mode={"router": "router", "quest": "quest", "topk": "topk"}[m], router_score="quest",
+                   router_mode="quantile", router_grain="row", router_quantile=0.25, budget_blocks=16, k_min=1,
+                   k_max=112)
+        policy = {"router": "router-on-Quest", "quest": "Quest", "topk": "K-mean top-k"}[m]
+    cfg = ops.SelectorConfig(**sel)
+    k_base, kmax = ops.budget(cfg, S)
+    model = decoder.TPDecoder(shape, cfg, world, rank, group=dist.group.WORLD if world > 1 else None,
+                              seed=0, device=dev)
+    gen = torch.Generator().manual_seed(1)
+    ids_host = torch.randint(0, shape.vocab, (S,), generator=gen).pin_memory()
+    ids = ids_host.to(dev)
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    def timed(n):
+        barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(n):
+            model.forward(ids)
+        b.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        t = torch.tensor([a.elapsed_time(b) / n], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
+    for _ in range(args.warmup):
+        model.forward(ids)
+    sampler = ClockSampler(dev.index if "CUDA_VISIBLE_DEVICES" not in os.environ else
+                           os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local])
+    sampler.start()
+    time.sleep(0.25)
+    ms = timed(args.steps)
+    clocks = sampler.stop()
+    # attention share of one forward (per-layer events; this rank)
+    model.events = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(shape.layers)]
+    model.forward(ids)
+    torch.cuda.synchronize()
+    attn_ms = sum(e[1].elapsed_time(e[2]) for e in model.events)
+    model.events = None
+    # end to end: token ids from pinned host memory, the last position's logits read back
+    vl = model.layout.vocab1 - model.layout.vocab0
+    host_out = torch.empty((vl,), dtype=torch.bfloat16).pin_memory()
+    barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(args.steps):
+        d_ids = ids_host.to(dev, non_blocking=True)
+        logits = model.forward(d_ids)
+        host_out.copy_(logits[-1], non_blocking=True)
+    b.record(stream)
+    torch.cuda.synchronize()
+    te = torch.tensor([a.elapsed_time(b) / args.steps], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_ms = te.item()
+    dense_ms = None
+    if not args.no_dense:
+        model.attention = "dense"
+        model.forward(ids)
+        dense_ms = timed(max(1, min(args.steps, 2)))
+        model.attention = "block_sparse"
+    flops = shape.gemm_flops(S) + shape.dense_attn_flops(S)
+    value = flops / (ms / 1e3) / 1e12
+    peaks, peak_kind = load_peaks()
+    peak = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    name = "Qwen2.5-7B" if args.workload == "cfg3" else "Qwen2.5-14B"
+    # tensor work actually done: the GEMMs, and the sparse attention at about its
+    # selected fraction (k_base..kmax of the visible blocks) -- the GEMMs dominate
+    line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (uniform random token ids, random-init weights)",
+            "config": {"workload": f"{args.workload}-{S // 1024}K: full prefill of a random-init {name}-shaped decoder "
+                                   f"({shape.layers} layers, hidden {shape.hidden}, {shape.heads}/{shape.kv_heads} "
+                                   f"heads, d{shape.head_dim}, MLP {shape.intermediate}, vocab {shape.vocab}), "
+                                   f"{policy} block 64 k_base={k_base} kmax={kmax} on every layer, "
+                                   f"tensor parallel over KV-head groups, NCCL all-reduce after o_proj and down_proj",
+                       "global_batch": 1, "seq_len": S, "parallelism": f"tp{world}" if world > 1 else "none",
+                       "l2": "activations and weights larger than L2"},
+            "prefill_ms": round(ms, 3), "tokens_per_s": round(S / (ms / 1e3), 1),
+            "attention_ms_rank0": round(attn_ms, 3),
+            "roofline": {"bound": "tensor", "kernel": "whole prefill (cuBLAS GEMMs + this package's attention)",
+                         "achieved": round(shape.gemm_flops(S) / (ms / 1e3) / 1e12, 2), "peak": peak,
+                         "unit": "TFLOP/s", "frac": round(shape.gemm_flops(S) / (ms / 1e3) / 1e12 / peak, 4),
+                         "peak_kind": f"bf16_tflops_sustained ({peak_kind})", "traffic": None,
+                         "note": "achieved counts the GEMM FLOPs only"},
+            "gpu_launches": None, "clocks": clocks,
+            "e2e": {"value": round(flops / (e2e_ms / 1e3) / 1e12, 3), "unit": UNIT,
+                    "h2d_bytes_per_step": S * 8, "d2h_bytes_per_step": vl * 2 * world, "ms_per_step": round(e2e_ms, 3)},
+            "cpu_baseline": None}
+    if dense_ms is not None:
+        line["dense_ms"] = round(dense_ms, 3)
+        line["dense_backend"] = "torch SDPA (enable_gqa), same model"
+        line["ratio_vs_dense"] = round(ms / dense_ms, 4)
     print(json.dumps(line), flush=True)
 
 
@@ -442,6 +601,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ugbsa", choices=["ugbsa", "reference"])
     ap.add_argument("--seq", type=int, default=131072)
+    ap.add_argument("--workload", default="attn-layer", choices=["attn-layer", "cfg5", "cfg3", "cfg4"],
+                    help="attn-layer: the metric's 28/4-head d128 layer; cfg5: BASELINE config 5 (d256, 16/2 heads); "
+                         "cfg3 / cfg4: full prefill of a Qwen2.5-7B / 14B-shaped decoder, tensor parallel")
+    ap.add_argument("--policy", default="router", choices=["router", "quest", "topk"],
+                    help="cfg4's selection policy (router-on-Quest, Quest, K-mean top-k)")
     ap.add_argument("--ref-tiles", type=int, default=32, help="tiles in the CPU sample")
     ap.add_argument("--no-dense", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -450,8 +614,17 @@ def main():
                     help="multi-GPU division of the layer (auto: grid when the ranks divide or are a multiple of "
                          "the KV heads, rows otherwise)")
     args = ap.parse_args()
+    global WORKLOAD
+    WORKLOAD = args.workload
     if args.warmup < 3 and args.impl == "ugbsa":
         args.warmup = 3
+    if args.workload in ("cfg3", "cfg4"):
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the full-model workloads have no CPU reference "
+                              "arm; the attention layer's is --workload attn-layer"}))
+            return
+        run_model(args)
+        return
     if args.impl == "reference":
         if int(os.environ.get("RANK", "0")) != 0:
             return

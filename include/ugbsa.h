@@ -329,6 +329,8 @@ int ugbsa_decode_attn(const void *q, const void *K, const void *V, int dtype, ug
  *   power of two, 16 <= rot_dim <= D), the rest pass through;
  *   Y [B, H, S, D] (may be X itself: each row is read before it is written).
  * norm_mode UGBSA_NORM_SCALE: y = T(w * T(x * r)) (Qwen3RMSNorm);
+ * UGBSA_NORM_NONE: y = x, no per-head norm (Qwen2 / Llama attention: rotary
+ * only; weight may be NULL);
  * UGBSA_NORM_OFFSET: y = T((x * r) * (1 + w)) (Qwen3.5-MoE / Qwen3-Next), with
  * r = 1 / sqrt(mean(fp32(x^2)) + eps); then out = T(T(y * cos) +
  * T(rotate_half(y) * sin)) on the rotated columns.  summary (for K):
@@ -339,6 +341,7 @@ int ugbsa_decode_attn(const void *q, const void *K, const void *V, int dtype, ug
 enum {
     UGBSA_NORM_SCALE = 0,
     UGBSA_NORM_OFFSET = 1,
+    UGBSA_NORM_NONE = 2,
     UGBSA_SUMMARY_NONE = 0,
     UGBSA_SUMMARY_MEAN = 1,
     UGBSA_SUMMARY_QUEST = 2

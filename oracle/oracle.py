@@ -443,12 +443,22 @@ def qk_norm_rope(x: np.ndarray, weight: np.ndarray, eps: float, cos: np.ndarray,
       r = 1 / sqrt(mean(fp32(x^2)) + eps)            (fp32)
       scale  (Qwen3RMSNorm):              y = T(w * T(x * r))
       offset (Qwen3.5-MoE / Qwen3-Next):  y = T((x * r) * (1 + w))
+      none   (Qwen2 / Llama, no per-head norm): y = x
       first R = cos.shape[-1] columns: T(T(y * cos) + T(rotate_half(y) * sin)); the rest y.
     x [B, H, S, D] float32 holding T values; weight [D]; cos / sin [B or 1, S, R].
     T rounding is emulated (round to nearest even)."""
     x = _f32(x)
-    w = np.asarray(weight, np.float32)
     D = x.shape[-1]
+    if norm_mode == "none":   # rotary only (Qwen2 / Llama attention)
+        y = x.copy()
+        R = cos.shape[-1]
+        c = np.asarray(cos, np.float32)[:, None]
+        s = np.asarray(sin, np.float32)[:, None]
+        yr = y[..., :R]
+        rot = np.concatenate([-yr[..., R // 2:], yr[..., :R // 2]], axis=-1)
+        y[..., :R] = _round(_round(yr * c, dtype) + _round(rot * s, dtype), dtype)
+        return y
+    w = np.asarray(weight, np.float32)
     sq = (x * x).astype(np.float32)
     var = (sq.sum(-1, keepdims=True, dtype=np.float32) / np.float32(D)).astype(np.float32)
     r = (np.float32(1.0) / np.sqrt((var + np.float32(eps)).astype(np.float32))).astype(np.float32)

@@ -213,7 +213,7 @@ def test_qk_norm_rope_validation_without_device():
     assert call(R=96) == 5            # rotated width: a power of two
     assert call(R=8) == 5
     assert call(dtype=_lib.F32) == 3
-    assert call(mode=2) == 1
+    assert call(mode=3) == 1          # modes: 0 scale, 1 offset, 2 none
     assert call(summary=3) == 1
     assert call(sa=None) == 1
     assert call(cs_s=100) == 4        # cos / sin rows not 16-byte aligned

@@ -46,6 +46,7 @@ CASES = [
     (2, 2, 1000, 256, 64, "offset", torch.bfloat16, "mean"),
     (1, 3, 777, 64, 32, "offset", torch.float16, "quest"),
     (2, 2, 512, 128, 16, "scale", torch.float16, None),
+    (1, 4, 1000, 128, 128, "none", torch.bfloat16, "quest"),   # Qwen2: rotary without a per-head norm
 ]
 
 
@@ -64,6 +65,8 @@ def test_norm_rope_matches_oracle(case):
     out, summ = (res if summary else (res, None))
     ok, same = _ulp_ok(out.float().cpu().numpy(), want, dtype)
     assert ok and same >= 0.999, same
+    if mode == "none":   # no sum of squares: every element bit-identical
+        assert same == 1.0
     if summary:
         ref = ops.block_summary(out, summary == "quest")
         if summary == "quest":

@@ -80,3 +80,35 @@ def test_round_to_bf16_matches_torch():
     x = np.random.default_rng(0).standard_normal(10000).astype(np.float32)
     t = torch.from_numpy(x).to(torch.bfloat16).float().numpy()
     assert np.array_equal(round_to_bf16(x), t)
+
+
+def test_decoder_tensor_parallel_layout_covers_everything_once():
+    """ugbsa.decoder.TPLayout: every Q head, KV head (replicated only when the ranks
+    outnumber the KV heads), intermediate column and vocab entry lands on a rank."""
+    from ugbsa import decoder
+    for shape in (decoder.QWEN25_7B, decoder.QWEN25_14B):
+        for world in (1, 2, 4, 8):
+            lays = [decoder.TPLayout.make(shape, world, r) for r in range(world)]
+            q = sorted((L.shard.q0, L.shard.q1) for L in lays)
+            assert q[0][0] == 0 and q[-1][1] == shape.heads
+            assert all(a[1] == b[0] for a, b in zip(q, q[1:]))
+            kv = {h for L in lays for h in range(L.shard.kv0, L.shard.kv1)}
+            assert kv == set(range(shape.kv_heads))
+            for L in lays:   # a rank's Q heads read only its KV heads
+                G = shape.heads // shape.kv_heads
+                assert L.shard.kv0 == L.shard.q0 // G and L.shard.kv1 == (L.shard.q1 - 1) // G + 1
+            inter = sorted((L.inter0, L.inter1) for L in lays)
+            assert inter[0][0] == 0 and inter[-1][1] == shape.intermediate
+            assert all(a[1] == b[0] for a, b in zip(inter, inter[1:]))
+            voc = sorted((L.vocab0, L.vocab1) for L in lays)
+            assert voc[0][0] == 0 and voc[-1][1] == shape.vocab
+            assert all(a[1] == b[0] for a, b in zip(voc, voc[1:]))
+
+
+def test_decoder_flop_counts():
+    from ugbsa import decoder
+    s = decoder.QWEN25_7B
+    # 7.07 B parameters in the linear layers and lm_head (embeddings excluded)
+    assert abs(s.gemm_flops(1) / 2 - 7.07e9) / 7.07e9 < 0.01
+    qt = 131072 // 64
+    assert s.dense_attn_flops(131072) == 28 * 28 * qt * (qt + 1) / 2 * 4 * 64 * 64 * 128

@@ -189,3 +189,52 @@ def test_two_gpu_grid_sharded_prefill_matches_single_gpu(tmp_path, grain, Hkv):
                        start_method="spawn")
     res = [open(tmp_path / f"r{r}.txt").read().split() for r in range(2)]
     assert all(r == ["1", "1"] for r in res), res
+
+
+def _tp_worker(rank, world, port, out_dir):
+    import datetime
+    import sys
+
+    import torch.distributed as dist
+    here = os.path.dirname(os.path.abspath(__file__))
+    repo = os.path.dirname(here)
+    for p in (os.path.join(repo, "uncertainty-gated-block-sparse-attention_b200"), repo):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    from ugbsa import decoder, ops
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    shape = decoder.DecoderShape(layers=2, hidden=512, heads=4, kv_heads=2, head_dim=128, intermediate=1024,
+                                 vocab=1000, rope_theta=1.0e6, rms_eps=1e-6)
+    cfg = ops.SelectorConfig(mode="router", router_score="quest", router_mode="quantile", router_grain="row",
+                             router_quantile=0.25, budget_blocks=2, k_min=1, k_max=112)
+    ids = torch.randint(0, shape.vocab, (2048,), generator=torch.Generator().manual_seed(5)).to(dev)
+    tp = decoder.TPDecoder(shape, cfg, world, rank, group=dist.group.WORLD, seed=3, device=dev)
+    got = tp.forward(ids).float()
+    one = decoder.TPDecoder(shape, cfg, 1, 0, seed=3, device=dev)
+    want = one.forward(ids)[:, tp.layout.vocab0:tp.layout.vocab1].float()
+    # the all-reduce adds the ranks' row-parallel partial sums in another order than one
+    # GEMM does: bf16 rounding differences, no more
+    top = want.abs().max().item()
+    d = (got - want).abs()
+    ok = d.max().item() <= 0.03 * top and d.mean().item() <= 0.003 * top
+    with open(os.path.join(out_dir, f"r{rank}.txt"), "w") as f:
+        f.write(f"{int(ok)} {d.max().item() / top:.3e}\n")
+    dist.barrier(device_ids=[rank])
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_gpu_tensor_parallel_decoder_matches_one_gpu(tmp_path):
+    """ugbsa.decoder over 2 ranks (one KV group each, NCCL all-reduce after o_proj and
+    down_proj) gives the 1-rank model's logits within bf16 rounding."""
+    port = _free_port()
+    mp.start_processes(_tp_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True, start_method="spawn")
+    res = [open(tmp_path / f"r{r}.txt").read().split() for r in range(2)]
+    assert all(r[0] == "1" for r in res), res

@@ -63,3 +63,19 @@ def test_norm_rope_matches_transformers(mode, D, R):
                               sin.float().numpy(), norm_mode=mode)
     ok, same = _ulp_ok(got, ref.float().numpy())
     assert ok and same >= 0.999, same
+
+
+@pytest.mark.parametrize("D", [128, 64])
+def test_rotary_only_matches_qwen2(D):
+    """norm_mode "none": Qwen2's attention rotates Q and K without a per-head
+    norm (transformers' modeling_qwen2.apply_rotary_pos_emb); bit for bit."""
+    from transformers.models.qwen2.modeling_qwen2 import apply_rotary_pos_emb
+    B, S, H = 2, 96, 3
+    g = torch.Generator().manual_seed(D)
+    x = (torch.randn(B, H, S, D, generator=g) * 3).to(torch.bfloat16)
+    cos, sin = _rope_tables(B, S, D, 11)
+    with torch.no_grad():
+        ref, _ = apply_rotary_pos_emb(x, x, cos, sin)
+    got = oracle.qk_norm_rope(x.float().numpy(), None, 0.0, cos.float().numpy(), sin.float().numpy(),
+                              norm_mode="none")
+    assert np.array_equal(got, ref.float().numpy())

@@ -390,18 +390,20 @@ int ugbsa_qk_norm_rope(const void *X, int dtype, ugbsa_strides xs, const void *w
     if (D != 64 && D != 128 && D != 256) return UGBSA_ERR_UNSUPPORTED;
     if (rot_dim < 16 || rot_dim > D || (rot_dim & (rot_dim - 1))) return UGBSA_ERR_UNSUPPORTED;
     if (dtype != UGBSA_BF16 && dtype != UGBSA_F16) return UGBSA_ERR_DTYPE;
-    if (norm_mode != UGBSA_NORM_SCALE && norm_mode != UGBSA_NORM_OFFSET) return UGBSA_ERR_ARG;
+    if (norm_mode != UGBSA_NORM_SCALE && norm_mode != UGBSA_NORM_OFFSET && norm_mode != UGBSA_NORM_NONE)
+        return UGBSA_ERR_ARG;
     if (summary < UGBSA_SUMMARY_NONE || summary > UGBSA_SUMMARY_QUEST) return UGBSA_ERR_ARG;
     if (!(eps >= 0.f)) return UGBSA_ERR_ARG;
     int rc;
     if ((rc = check_view(X, dtype, xs)) || (rc = check_view(Y, dtype, ys))) return rc;
-    if (!weight || !cos || !sin) return UGBSA_ERR_ARG;
-    if (!aligned16(weight) || !aligned16(cos) || !aligned16(sin)) return UGBSA_ERR_ALIGN;
+    const bool has_w = norm_mode != UGBSA_NORM_NONE;
+    if ((has_w && !weight) || !cos || !sin) return UGBSA_ERR_ARG;
+    if ((has_w && !aligned16(weight)) || !aligned16(cos) || !aligned16(sin)) return UGBSA_ERR_ALIGN;
     if (cs_b < 0 || cs_s < rot_dim || (cs_b * 2) % 16 || (cs_s * 2) % 16) return UGBSA_ERR_ALIGN;
     if (summary && (!summ_a || (summary == UGBSA_SUMMARY_QUEST && !summ_b))) return UGBSA_ERR_ARG;
     if (summary && (!aligned16(summ_a) || (summary == UGBSA_SUMMARY_QUEST && !aligned16(summ_b))))
         return UGBSA_ERR_ALIGN;
-    return launch_qk_norm_rope(X, dtype, xs, weight, norm_mode == UGBSA_NORM_OFFSET ? 1 : 0, eps, cos, sin, cs_b,
+    return launch_qk_norm_rope(X, dtype, xs, weight, norm_mode == UGBSA_NORM_NONE ? 2 : (norm_mode == UGBSA_NORM_OFFSET ? 1 : 0), eps, cos, sin, cs_b,
                                cs_s, rot_dim, B, H, S, D, Y, ys, summary, summ_a, summ_b,
                                reinterpret_cast<cudaStream_t>(stream));
 }

@@ -12,6 +12,7 @@
 //   v    = sum_d fp32(x_d^2) / D in fp32, r = 1 / sqrt(v + eps)
 //   mode SCALE  (Qwen3 / Llama RMSNorm):  y = T(w * T(x * r))
 //   mode OFFSET (Qwen3.5 / Qwen3-Next):   y = T((x * r) * (1 + w))
+//   mode NONE   (Qwen2 / Llama: rotary without a per-head norm):  y = x
 //   rotary dims d < R (R = cos / sin width):
 //     out_d = T(T(y_d * cos_d) + T(rot_d * sin_d)),  rot_d = -y_{d+R/2} (d < R/2), y_{d-R/2} (else)
 //   d >= R: out_d = y_d
@@ -62,7 +63,7 @@ __device__ __forceinline__ T2 to_pair(float a, float b) {
 
 struct RopeParams {
     int B, H, S, D, NB, R;
-    int offset_mode;   // 1: y = (x r)(1 + w), 0: y = w T(x r)
+    int norm_mode;     // 0: y = w T(x r), 1: y = (x r)(1 + w), 2: y = x (no norm, W unused)
     float eps;
     int64_t xb, xh, xs, yb, yh, ys, cb, cs;
     int summary;       // 0 none, 1 mean, 2 Quest
@@ -114,9 +115,12 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(const T *__restrict__
         }
     }
     using T2 = typename std::conditional<std::is_same<T, __nv_bfloat16>::value, __nv_bfloat162, __half2>::type;
-    float w[8];
-    ld8(W + d0, w);
-    const uint4 wraw = __ldg(reinterpret_cast<const uint4 *>(W + d0));
+    float w[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    uint4 wraw = make_uint4(0u, 0u, 0u, 0u);
+    if (p.norm_mode != 2) {
+        ld8(W + d0, w);
+        wraw = __ldg(reinterpret_cast<const uint4 *>(W + d0));
+    }
     const T2 *w2 = reinterpret_cast<const T2 *>(&wraw);
     float w1[8];   // 1 + w (offset mode), fp32 as the reference's weight.float()
 #pragma unroll
@@ -166,10 +170,15 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(const T *__restrict__
             // D is a power of two: the mean's division is an exact scaling
             const float rs = 1.0f / sqrtf(__fadd_rn(__fmul_rn(ss, 1.0f / (float)D), p.eps));
             uint32_t yv[4];
+            const uint32_t xw[4] = {xa[ps].x, xa[ps].y, xa[ps].z, xa[ps].w};
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 T2 v;
-                if (p.offset_mode) {
+                if (p.norm_mode == 2) {
+                    yv[i] = xw[i];   // no norm: the input pairs as they are
+                    continue;
+                }
+                if (p.norm_mode == 1) {
                     v = to_pair<T2>(__fmul_rn(__fmul_rn(x[2 * i], rs), w1[2 * i]),
                                     __fmul_rn(__fmul_rn(x[2 * i + 1], rs), w1[2 * i + 1]));
                 } else {
@@ -255,13 +264,13 @@ static int launch_rope_t(const void *X, const void *weight, const void *cos, con
     return cudaGetLastError() == cudaSuccess ? UGBSA_OK : UGBSA_ERR_LAUNCH;
 }
 
-int launch_qk_norm_rope(const void *X, int dtype, ugbsa_strides xs, const void *weight, int offset_mode, float eps,
+int launch_qk_norm_rope(const void *X, int dtype, ugbsa_strides xs, const void *weight, int norm_mode, float eps,
                         const void *cos, const void *sin, int64_t cs_b, int64_t cs_s, int rot_dim, int B, int H,
                         int S, int D, void *Y, ugbsa_strides ys, int summary, float *summ_a, float *summ_b,
                         cudaStream_t stream) {
     RopeParams p;
     p.B = B; p.H = H; p.S = S; p.D = D; p.NB = (S + 63) / 64; p.R = rot_dim;
-    p.offset_mode = offset_mode;
+    p.norm_mode = norm_mode;
     p.eps = eps;
     p.xb = xs.b; p.xh = xs.h; p.xs = xs.s;
     p.yb = ys.b; p.yh = ys.h; p.ys = ys.s;

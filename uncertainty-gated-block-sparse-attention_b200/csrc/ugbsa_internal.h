@@ -54,7 +54,8 @@ int launch_select(const void *Q, int dtype, ugbsa_strides qs, const float *summ_
                   int32_t *kv_idx, float *sigma_out, uint8_t *trigger_out, void *workspace, cudaStream_t stream);
 
 // fused per-head RMSNorm + rotary embedding (+ K block summary) (rope.cu)
-int launch_qk_norm_rope(const void *X, int dtype, ugbsa_strides xs, const void *weight, int offset_mode, float eps,
+// norm_mode: 0 scale, 1 offset, 2 none (weight unused)
+int launch_qk_norm_rope(const void *X, int dtype, ugbsa_strides xs, const void *weight, int norm_mode, float eps,
                         const void *cos, const void *sin, int64_t cs_b, int64_t cs_s, int rot_dim, int B, int H,
                         int S, int D, void *Y, ugbsa_strides ys, int summary, float *summ_a, float *summ_b,
                         cudaStream_t stream);

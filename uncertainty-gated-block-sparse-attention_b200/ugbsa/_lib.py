@@ -20,7 +20,7 @@ MODE = {"topk": 0, "quest": 1, "router": 2}
 SCORE = {"mean": 0, "quest": 1}
 ROUTER_MODE = {"abs": 0, "quantile": 1}
 GRAIN = {"cell": 0, "row": 1}
-NORM_SCALE, NORM_OFFSET = 0, 1
+NORM_SCALE, NORM_OFFSET, NORM_NONE = 0, 1, 2
 
 
 class Strides(ctypes.Structure):

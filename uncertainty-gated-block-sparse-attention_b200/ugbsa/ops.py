@@ -283,14 +283,18 @@ def qk_norm_rope(x: torch.Tensor, weight: torch.Tensor, eps: float, cos: torch.T
 
     x [B,H,S,D] bf16/fp16 view (e.g. proj.view(B,S,H,D).transpose(1,2));
     weight [D]; cos/sin [B or 1, S, R] (R rotated columns).  norm_mode
-    "scale" (Qwen3RMSNorm) or "offset" (Qwen3.5-MoE / Qwen3-Next, 1 + w).
+    "scale" (Qwen3RMSNorm), "offset" (Qwen3.5-MoE / Qwen3-Next, 1 + w) or
+    "none" (rotary only, Qwen2 / Llama attention; ``weight`` may be None).
     ``out`` [B,H,S,D] view (default: new contiguous; ``x`` itself works).
     summary "mean" / "quest": also returns the block summaries of the output
     (as block_summary(out, ...) would): (out, summ).
     """
-    _need_cuda(x, weight, cos, sin)
-    if x.dtype not in (torch.bfloat16, torch.float16) or weight.dtype != x.dtype or cos.dtype != x.dtype \
-            or sin.dtype != x.dtype:
+    if norm_mode == "none":
+        _need_cuda(x, cos, sin)
+    else:
+        _need_cuda(x, weight, cos, sin)
+    if x.dtype not in (torch.bfloat16, torch.float16) or (weight is not None and weight.dtype != x.dtype) \
+            or cos.dtype != x.dtype or sin.dtype != x.dtype:
         raise ValueError("x, weight, cos and sin must share one dtype (bf16 or fp16)")
     B, H, S, D = x.shape
     if cos.dim() == 2:
@@ -300,12 +304,12 @@ def qk_norm_rope(x: torch.Tensor, weight: torch.Tensor, eps: float, cos: torch.T
         raise ValueError("cos/sin must be [B or 1, S, R] with unit innermost stride and equal strides")
     R = cos.shape[-1]
     x = _inner_contig(x)
-    weight = weight.contiguous()
+    weight = weight.contiguous() if norm_mode != "none" else None
     if out is None:
         out = torch.empty((B, H, S, D), device=x.device, dtype=x.dtype)
     elif tuple(out.shape) != (B, H, S, D) or out.dtype != x.dtype or out.stride(-1) != 1:
         raise ValueError("out must be a [B,H,S,D] view with unit innermost stride")
-    mode = {"scale": _lib.NORM_SCALE, "offset": _lib.NORM_OFFSET}[norm_mode]
+    mode = {"scale": _lib.NORM_SCALE, "offset": _lib.NORM_OFFSET, "none": _lib.NORM_NONE}[norm_mode]
     sm = {None: 0, "mean": 1, "quest": 2}[summary]
     nb = math.ceil(S / BLOCK)
     sa = torch.empty((B, H, nb, D), device=x.device, dtype=torch.float32) if sm else None
