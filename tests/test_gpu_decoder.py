@@ -33,7 +33,12 @@ def _hf_model(run: decoder.TPDecoder, attn_impl: str):
                       rope_parameters={"rope_type": "default", "rope_theta": s.rope_theta}, rms_norm_eps=s.rms_eps,
                       max_position_embeddings=8192, tie_word_embeddings=False)
     cfg._attn_implementation = attn_impl
-    m = Qwen2ForCausalLM(cfg).to(DEV).to(torch.bfloat16).eval()
+    m = Qwen2ForCausalLM(cfg)
+    inv_freq = m.model.rotary_emb.inv_freq.clone()          # fp32
+    m = m.to(DEV).to(torch.bfloat16).eval()
+    # .to(bfloat16) also rounds the rotary frequencies (a buffer) to bf16, which a
+    # model loaded with torch_dtype=bfloat16 keeps in fp32: restore them
+    m.model.rotary_emb.inv_freq = inv_freq.to(DEV)
     H, Hk, D, I = s.heads, s.kv_heads, s.head_dim, s.intermediate
     with torch.no_grad():
         m.model.embed_tokens.weight.copy_(run.embed)
