@@ -380,6 +380,51 @@ int ugbsa_block_order_stats(const void *Q, int dtype, ugbsa_strides qs, const fl
                             size_t workspace_bytes, ugbsa_stream_t stream);
 
 /*
+ * The v1 per-row selector and its attention (the reference's _block_select_mask,
+ * src/sparse_attention.py:208-382, modes topk / quest / router, and its v1
+ * kernel block_sparse_attn with the per-row inner mask,
+ * src/triton_block_attn.py:39-181).  Every query row ranks, by its own fp32
+ * score (the canonical order of ugbsa_select), the blocks that start at or
+ * before it and keeps the top k_bud = clamp(budget_blocks, k_min, k_max)
+ * (ties to the lower block id), plus the sink and its own block.  Router: the
+ * row's margin on its raw scores at k_eff = clamp(budget_blocks, 1, NB-1),
+ * rows with more than k_eff visible blocks eligible, row grain = head mean,
+ * quantile over the eligible cells (ineligible and NaN as +inf, k =
+ * int(q * eligible count), the row-grain count being of rows) or abs
+ * threshold; a triggered (head, row) keeps every visible block.
+ *
+ * ugbsa_select_rows: Q [B, Hq, S, D]; summaries as for ugbsa_select;
+ *   keep_bits [B, Hq, S, ceil(NB/32)] uint32 out (bit j of a row: block j kept);
+ *   kv_idx (optional) [B, Hq, ceil(S/64), NB] int32 out: per tile the union of
+ *   its rows' blocks, ascending, then the sentinel NB;  sigma (optional)
+ *   [B, Hq, S] fp32: the margin after the grain step that the threshold is
+ *   compared with (+inf for ineligible rows; NaN without the router);
+ *   trigger (optional) [B, Hq, S] uint8.  NB <= 6144.  Workspace:
+ *   ugbsa_select_rows_workspace_bytes (the per-row scores, 4*B*Hq*S*NB bytes,
+ *   as the reference materialises them).
+ * ugbsa_keep_to_tiles: a caller's keep mask keep [B, H, S, NB] uint8 (or NULL
+ *   when keep_bits already holds the bits) -> keep_bits, and kv_idx as above
+ *   (NULL to skip).
+ * ugbsa_attn_rowmask: attention over kv_idx (kmax slots, NB for the lists
+ *   above) where row m uses a listed block only if its bit in keep_bits
+ *   [B, Hq, S, ceil(NB/32)] is set; bf16 / fp16, head_dim 64 / 128 / 256, the
+ *   whole sequence (Sq = Sk = S).
+ */
+size_t ugbsa_select_rows_workspace_bytes(const ugbsa_selector_config *cfg, int B, int Hq, int S);
+
+int ugbsa_select_rows(const void *Q, int dtype, ugbsa_strides qs, const float *summ_a, const float *summ_b, int B,
+                      int Hq, int Hkv, int S, int D, float scale, const ugbsa_selector_config *cfg,
+                      uint32_t *keep_bits, int32_t *kv_idx, float *sigma, uint8_t *trigger, void *workspace,
+                      size_t workspace_bytes, ugbsa_stream_t stream);
+
+int ugbsa_keep_to_tiles(const uint8_t *keep, uint32_t *keep_bits, int B, int H, int S, int32_t *kv_idx,
+                        ugbsa_stream_t stream);
+
+int ugbsa_attn_rowmask(const void *Q, const void *K, const void *V, int dtype, ugbsa_strides qs, ugbsa_strides ks,
+                       ugbsa_strides vs, const int32_t *kv_idx, int kmax, const uint32_t *keep_bits, int B, int Hq,
+                       int Hkv, int S, int D, float scale, void *out, ugbsa_strides os, ugbsa_stream_t stream);
+
+/*
  * Reads and clears the library's device-side error word (a host sync on the
  * given stream).  Returns UGBSA_OK, or UGBSA_ERR_DEVICE if a kernel gave up on
  * a bounded wait since the last call; *bits (optional) receives the raw bits.

@@ -92,6 +92,9 @@ def lib():
         L.oracle_rank_tiles_range.argtypes = [P, I, I, I, ctypes.POINTER(_Cfg), I, I, P, P]
         L.oracle_attn_range.argtypes = ([P, I64, I64, I64, I64] * 3) + [P, I, I, I, I, I, I, I, F, I, I, P]
         L.oracle_decode_scores.argtypes = [P, I64, I64, I64, P, P, I, I, I, I, I, I, F, I, P]
+        L.oracle_row_scores.argtypes = [P, I64, I64, I64, I64, P, P, I, I, I, I, I, F, I, P]
+        L.oracle_select_rows_from_scores.argtypes = [P, I, I, I, ctypes.POINTER(_Cfg), P, P, P, P, P]
+        L.oracle_attn_keep.argtypes = ([P, I64, I64, I64, I64] * 3) + [P, I, I, I, I, I, I, F, P]
         L.oracle_set_threads.argtypes = [I]
         L.oracle_set_threads.restype = None
         L.oracle_get_threads.argtypes = []
@@ -306,6 +309,64 @@ def router_from_cells(cells: np.ndarray, cfg: OracleConfig) -> dict:
         thresh = np.float32(cfg.router_tau)
         trig = eff < thresh
     return {"sigma_eff": eff, "thresh": np.float32(thresh), "trigger": trig}
+
+
+def row_scores(q: np.ndarray, summ, scale: float, quest: bool) -> np.ndarray:
+    """Per-row block scores [B,Hq,S,NB] (-inf where the block starts after the row),
+    the v1 selector's score matrix (src/sparse_attention.py:221-244) in the canonical order."""
+    q = _f32(q)
+    B, Hq, S, D = q.shape
+    sa, sb = (summ if quest else (summ, None))
+    sa = _f32(sa)
+    sb = _f32(sb) if sb is not None else None
+    nb = math.ceil(S / BLOCK)
+    rs = np.empty((B, Hq, S, nb), np.float32)
+    rc = lib().oracle_row_scores(_ptr(q), Hq * S * D, S * D, D, 1, _ptr(sa), _ptr(sb) if quest else None, B, Hq,
+                                 sa.shape[1], S, D, ctypes.c_float(scale), int(quest), _ptr(rs))
+    assert rc == 0
+    return rs
+
+
+def select_rows_from_scores(rs: np.ndarray, cfg: OracleConfig) -> dict:
+    """v1 per-row selection from per-row scores (src/sparse_attention.py:245-352):
+    keep [B,H,S,NB] bool, per-(head, row) margins, margins after the grain step,
+    triggers and the quantile threshold."""
+    rs = _f32(rs)
+    B, H, S, nb = rs.shape
+    keep = np.empty((B, H, S, nb), np.uint8)
+    sig = np.empty((B, H, S), np.float32)
+    eff = np.empty((B, H, S), np.float32)
+    trig = np.empty((B, H, S), np.uint8)
+    th = np.empty((1,), np.float32)
+    rc = lib().oracle_select_rows_from_scores(_ptr(rs), B, H, S, ctypes.byref(cfg.c()), _ptr(keep), _ptr(sig),
+                                              _ptr(eff), _ptr(trig), _ptr(th))
+    assert rc == 0
+    return {"keep": keep.astype(bool), "sigma": sig, "sigma_eff": eff, "trigger": trig.astype(bool),
+            "thresh": float(th[0])}
+
+
+def select_rows(q: np.ndarray, k: np.ndarray, scale: float, cfg: OracleConfig) -> dict:
+    """The whole v1 selection: summaries -> per-row scores -> keep (+ router state)."""
+    summ = block_summary(k, cfg.quest)
+    rs = row_scores(q, summ, scale, cfg.quest)
+    out = select_rows_from_scores(rs, cfg)
+    out["row_scores"] = rs
+    return out
+
+
+def attn_keep(q, k, v, keep, scale: float) -> np.ndarray:
+    """Attention with a per-row keep mask [B,Hq,S,NB] (the v1 kernel's semantics,
+    src/triton_block_attn.py:39-122), float64 accumulation, float32 out."""
+    q, k, v = _f32(q), _f32(k), _f32(v)
+    keep = np.ascontiguousarray(keep, dtype=np.uint8)
+    B, Hq, Sq, D = q.shape
+    Hkv, Sk = k.shape[1], k.shape[2]
+    out = np.empty((B, Hq, Sq, D), np.float32)
+    rc = lib().oracle_attn_keep(_ptr(q), Hq * Sq * D, Sq * D, D, 1, _ptr(k), Hkv * Sk * D, Sk * D, D, 1,
+                                _ptr(v), Hkv * Sk * D, Sk * D, D, 1, _ptr(keep), B, Hq, Hkv, Sq, Sk, D,
+                                ctypes.c_float(scale), _ptr(out))
+    assert rc == 0
+    return out
 
 
 def canonical_sets(kv_idx: np.ndarray, S: int):

@@ -503,3 +503,216 @@ int oracle_decode_scores(const float *Q, int64_t qb, int64_t qh, int64_t qd, con
         }
     return 0;
 }
+
+/* -------------------------------------------------------------------------- */
+/* v1 per-row selection: sparse_attention.py:208-382 (_block_select_mask),    */
+/* modes topk / quest / router, and the per-row keep mask of its kernel        */
+/* (triton_block_attn.py:39-122).  Every query row r (Q == K, prefill) ranks   */
+/* the blocks that start at or before r by its own fp32 score (the canonical   */
+/* chains above, :221-239), keeps the top k_bud = clamp(budget, k_min, k_max)  */
+/* (ties to the lower block id), then the sink and its own block (:281-283).   */
+/* Router (:295-352): per-(head, row) margin of the RAW scores at             */
+/* k_eff = clamp(budget, 1, NB-1); rows with more than k_eff visible blocks    */
+/* are eligible; row grain averages over heads; quantile over the eligible    */
+/* cells (ineligible and NaN as +inf, k = int(q * eligible count) where the    */
+/* row-grain count is of rows, not batch x rows, :331-335); triggered cells    */
+/* keep every visible block.                                                   */
+/* -------------------------------------------------------------------------- */
+
+/* rs [B,H,S,NB]: row r's score of block j, -inf where block j starts after r */
+int oracle_row_scores(const float *Q, int64_t sb, int64_t sh, int64_t ss, int64_t sd,
+                      const float *summ_a, const float *summ_b,
+                      int B, int Hq, int Hkv, int S, int D, float scale, int quest, float *rs) {
+    if (B <= 0 || Hq <= 0 || Hkv <= 0 || S <= 0 || D <= 0 || Hq % Hkv) return 1;
+    const int NB = (int)cdiv64(S, BLK);
+    const int G = Hq / Hkv;
+#pragma omp parallel for collapse(3) schedule(dynamic, 64)
+    for (int b = 0; b < B; ++b)
+        for (int h = 0; h < Hq; ++h)
+            for (int r = 0; r < S; ++r) {
+                const int kvh = h / G;
+                const float *A = summ_a + ((int64_t)b * Hkv + kvh) * NB * D;
+                const float *Bm = quest ? summ_b + ((int64_t)b * Hkv + kvh) * NB * D : NULL;
+                const float *q = Q + b * sb + h * sh + (int64_t)r * ss;
+                float *row = rs + (((int64_t)b * Hq + h) * S + r) * NB;
+                const int nvis = r / BLK + 1;
+                for (int j = 0; j < NB; ++j) {
+                    if (j >= nvis) { row[j] = -INFINITY; continue; }
+                    if (!quest) {
+                        float acc = 0.0f;
+                        for (int d = 0; d < D; ++d) acc = fmaf(q[d * sd], A[(int64_t)j * D + d], acc);
+                        row[j] = acc * scale;
+                    } else {
+                        float ap = 0.0f, an = 0.0f;
+                        for (int d = 0; d < D; ++d) {
+                            const float x = q[d * sd];
+                            ap = fmaf(x > 0.0f ? x : 0.0f, Bm[(int64_t)j * D + d], ap);
+                            an = fmaf(x < 0.0f ? x : 0.0f, A[(int64_t)j * D + d], an);
+                        }
+                        row[j] = (ap + an) * scale;
+                    }
+                }
+            }
+    return 0;
+}
+
+/* keep [B,H,S,NB] uint8 out; sigma / eff [B,H,S] (NaN unless router); trig [B,H,S];
+ * thresh_out: the quantile threshold (NaN when none), fp32(tau) in abs mode. */
+int oracle_select_rows_from_scores(const float *rs, int B, int H, int S, const oracle_cfg *c, uint8_t *keep,
+                                   float *sigma, float *eff_out, uint8_t *trig, float *thresh_out) {
+    if (B <= 0 || H <= 0 || S <= 0) return 1;
+    const int NB = (int)cdiv64(S, BLK);
+    int kb = c->budget_blocks < c->k_max ? c->budget_blocks : c->k_max;   /* :268 */
+    kb = kb > c->k_min ? kb : c->k_min;
+    if (kb > NB) kb = NB;
+    const int router = c->mode == 2;
+    int keff = c->budget_blocks < NB - 1 ? c->budget_blocks : NB - 1;       /* :303-304 */
+    if (keff < 1) keff = 1;
+    const int64_t ncell = (int64_t)B * H * S;
+    float *sig = (float *)malloc(sizeof(float) * (size_t)ncell);
+#pragma omp parallel for schedule(dynamic, 64)
+    for (int64_t cell = 0; cell < ncell; ++cell) {
+        const int r = (int)(cell % S);
+        const float *row = rs + cell * NB;
+        uint8_t *kp = keep + cell * NB;
+        vi_t *a = (vi_t *)malloc(sizeof(vi_t) * NB);
+        for (int j = 0; j < NB; ++j) { a[j].v = row[j] + 0.0f; a[j].i = j; }
+        qsort(a, NB, sizeof(vi_t), cmp_desc);
+        memset(kp, 0, (size_t)NB);
+        for (int j = 0; j < kb; ++j) kp[a[j].i] = 1;
+        kp[0] = 1;                 /* :282 */
+        kp[r / BLK] = 1;           /* :283 */
+        float s = NAN;
+        if (router) {
+            const float s_top = a[0].v, s_km1 = a[keff - 1].v, s_k = a[keff].v;
+            float spread = s_top - s_k;
+            if (spread < 1e-6f) spread = 1e-6f;
+            s = (s_km1 - s_k) / spread;
+        }
+        sig[cell] = s;
+        free(a);
+    }
+    float thresh = NAN;
+    float *eff = (float *)malloc(sizeof(float) * (size_t)ncell);
+    uint8_t *unc = (uint8_t *)calloc((size_t)ncell, 1);
+    if (router) {
+        const int row_grain = c->router_grain == 1;
+        /* eligibility is per row: more than k_eff visible blocks */
+        int64_t n_elig_rows = 0;
+        for (int r = 0; r < S; ++r) n_elig_rows += (r / BLK + 1) > keff;
+        for (int b = 0; b < B; ++b)
+            for (int r = 0; r < S; ++r) {
+                if (row_grain) {
+                    float acc = 0.0f;
+                    for (int h = 0; h < H; ++h) acc = acc + sig[((int64_t)b * H + h) * S + r];
+                    const float m = acc / (float)H;
+                    for (int h = 0; h < H; ++h) eff[((int64_t)b * H + h) * S + r] = m;
+                } else {
+                    for (int h = 0; h < H; ++h) eff[((int64_t)b * H + h) * S + r] = sig[((int64_t)b * H + h) * S + r];
+                }
+            }
+        if (c->router_mode == 1) {
+            /* the scored cells: [B,1,S] for row grain, [B,H,S] for cell grain */
+            const int64_t n = row_grain ? (int64_t)B * S : ncell;
+            const int64_t n_elig = row_grain ? n_elig_rows : (int64_t)B * H * n_elig_rows;
+            float *v = (float *)malloc(sizeof(float) * (size_t)n);
+            for (int64_t i = 0; i < n; ++i) {
+                const int64_t src = row_grain ? ((i / S) * H) * S + (i % S) : i;
+                const int r = (int)(i % S);
+                const float m = eff[src];
+                v[i] = ((r / BLK + 1) > keff && !isnan(m)) ? m : INFINITY;
+            }
+            int64_t kq = n_elig > 0 ? (int64_t)(c->router_quantile * (double)n_elig) : 0;
+            if (n_elig > 0 && kq < 1) kq = 1;
+            if (kq > 0) {
+                float *sorted = (float *)malloc(sizeof(float) * (size_t)n);
+                memcpy(sorted, v, sizeof(float) * (size_t)n);
+                qsort(sorted, n, sizeof(float), cmp_asc_nanlast);
+                thresh = sorted[kq - 1];
+                free(sorted);
+                for (int64_t cell = 0; cell < ncell; ++cell) {
+                    const int r = (int)(cell % S);
+                    const int64_t i = row_grain ? (cell / ((int64_t)H * S)) * S + r : cell;
+                    unc[cell] = (r / BLK + 1) > keff && v[i] <= thresh;
+                }
+            }
+            free(v);
+        } else {
+            thresh = (float)c->router_tau;
+            for (int64_t cell = 0; cell < ncell; ++cell) {
+                const int r = (int)(cell % S);
+                unc[cell] = (r / BLK + 1) > keff && eff[cell] < thresh;
+            }
+        }
+        for (int64_t cell = 0; cell < ncell; ++cell)
+            if (unc[cell]) {   /* dense row: every visible block (:345-347) */
+                const int r = (int)(cell % S);
+                uint8_t *kp = keep + cell * NB;
+                for (int j = 0; j < NB; ++j) kp[j] = (j * BLK <= r);
+            }
+    } else {
+        for (int64_t i = 0; i < ncell; ++i) eff[i] = NAN;
+    }
+    if (sigma) memcpy(sigma, sig, sizeof(float) * (size_t)ncell);
+    if (eff_out) memcpy(eff_out, eff, sizeof(float) * (size_t)ncell);
+    if (trig) memcpy(trig, unc, (size_t)ncell);
+    if (thresh_out) *thresh_out = thresh;
+    free(sig); free(eff); free(unc);
+    return 0;
+}
+
+/* Attention with a per-row keep mask (triton_block_attn.py:39-122): row m uses
+ * key n iff keep[b,h,m,n/64], n <= m and n < Sk; float64 accumulation; rows with
+ * no usable key give 0.  keep [B,Hq,Sq,NB] uint8; out [B,Hq,Sq,D] dense. */
+int oracle_attn_keep(const float *Q, int64_t qb, int64_t qh, int64_t qs, int64_t qd,
+                     const float *K, int64_t kb_, int64_t kh, int64_t ks, int64_t kd,
+                     const float *V, int64_t vb, int64_t vh, int64_t vs, int64_t vd,
+                     const uint8_t *keep, int B, int Hq, int Hkv, int Sq, int Sk, int D, float scale, float *out) {
+    if (B <= 0 || Hq <= 0 || Hkv <= 0 || Sq <= 0 || Sk <= 0 || D <= 0 || Hq % Hkv) return 1;
+    const int NB = (int)cdiv64(Sk, BLK);
+    const int G = Hq / Hkv;
+    const int64_t nrows = (int64_t)B * Hq * Sq;
+#pragma omp parallel
+    {
+        double *logit = (double *)malloc(sizeof(double) * (size_t)Sk);
+        double *acc = (double *)malloc(sizeof(double) * D);
+#pragma omp for schedule(dynamic, 16)
+        for (int64_t it = 0; it < nrows; ++it) {
+            const int m = (int)(it % Sq);
+            const int h = (int)((it / Sq) % Hq);
+            const int b = (int)(it / ((int64_t)Sq * Hq));
+            const int kvh = h / G;
+            const uint8_t *kp = keep + it * NB;
+            const float *q = Q + b * qb + h * qh + (int64_t)m * qs;
+            double mx = -INFINITY;
+            int n_used = 0;
+            for (int n = 0; n <= m && n < Sk; ++n) {
+                if (!kp[n / BLK]) { logit[n] = NAN; continue; }
+                const float *k = K + b * kb_ + kvh * kh + (int64_t)n * ks;
+                double dot = 0.0;
+                for (int d = 0; d < D; ++d) dot += (double)q[d * qd] * (double)k[d * kd];
+                dot *= (double)scale;
+                logit[n] = dot;
+                if (dot > mx) mx = dot;
+                ++n_used;
+            }
+            float *o = out + it * D;
+            if (n_used == 0) {
+                for (int d = 0; d < D; ++d) o[d] = 0.0f;
+                continue;
+            }
+            double l = 0.0;
+            for (int d = 0; d < D; ++d) acc[d] = 0.0;
+            for (int n = 0; n <= m && n < Sk; ++n) {
+                if (!kp[n / BLK]) continue;
+                const double p = exp(logit[n] - mx);
+                l += p;
+                const float *v = V + b * vb + kvh * vh + (int64_t)n * vs;
+                for (int d = 0; d < D; ++d) acc[d] += p * (double)v[d * vd];
+            }
+            for (int d = 0; d < D; ++d) o[d] = (float)(acc[d] / l);
+        }
+        free(logit); free(acc);
+    }
+    return 0;
+}

@@ -33,6 +33,12 @@ tests/golden/configs/ (``CONFIG_CASES``):
   scored in fp32, Quest router, k_base 32, 16 chained planted blocks): the
   canonical block sets as a packed bit mask, the per-head margins, the quantile
   and the log diagnostics (its tile scores, 29 MB, are not stored).
+
+``--v1`` records the reference's v1 per-row selector ``_block_select_mask``
+(src/sparse_attention.py:208-382) into tests/golden/v1/ (``V1_CASES``): the
+keep mask (packed bits), the per-row scores it ranks (captured at its first
+topk), the router's masked margins, quantile and threshold, the SEL.log
+records, and reference_attn on the keep mask for the attention cases.
 """
 from __future__ import annotations
 
@@ -123,6 +129,115 @@ def pack_sets(kv_idx: np.ndarray, S: int) -> np.ndarray:
     b, h, t, j = np.nonzero(ok)
     mask[b, h, t, ids[b, h, t, j]] = True
     return np.packbits(mask, axis=-1)
+
+
+# v1 per-row selection (src/sparse_attention.py:208-382) + reference_attn with its keep mask
+V1_CASES = {
+    "v1_topk_mean": dict(
+        inp=dict(B=1, Hq=4, Hkv=4, S=1024, D=64, n_planted=4, seed=61, chained=False, bf16=False),
+        sel=dict(mode="topk", router_score="mean", router_mode="quantile", router_grain="row",
+                 router_quantile=0.25, budget_blocks=4, k_min=1, k_max=112), attn=True),
+    "v1_quest_gqa_bf16": dict(
+        inp=dict(B=1, Hq=4, Hkv=2, S=1024, D=64, n_planted=4, seed=62, chained=True, bf16=True),
+        sel=dict(mode="quest", router_score="mean", router_mode="quantile", router_grain="row",
+                 router_quantile=0.25, budget_blocks=3, k_min=1, k_max=112), attn=False),
+    "v1_router_row_quantile": dict(
+        inp=dict(B=1, Hq=4, Hkv=4, S=1024, D=64, n_planted=4, seed=63, chained=False, bf16=False),
+        sel=dict(mode="router", router_score="mean", router_mode="quantile", router_grain="row",
+                 router_quantile=0.25, budget_blocks=4, k_min=1, k_max=112), attn=True),
+    "v1_router_cell_quest": dict(
+        inp=dict(B=1, Hq=3, Hkv=3, S=1024, D=64, n_planted=4, seed=64, chained=False, bf16=False),
+        sel=dict(mode="router", router_score="quest", router_mode="quantile", router_grain="cell",
+                 router_quantile=0.3, budget_blocks=4, k_min=1, k_max=112), attn=False),
+    "v1_router_abs_row": dict(
+        inp=dict(B=1, Hq=2, Hkv=2, S=1024, D=64, n_planted=4, seed=65, chained=False, bf16=False),
+        sel=dict(mode="router", router_score="mean", router_mode="abs", router_grain="row",
+                 router_quantile=0.25, router_tau=0.05, budget_blocks=4, k_min=1, k_max=112), attn=False),
+    "v1_router_batch2_ragged": dict(
+        inp=dict(B=2, Hq=2, Hkv=1, S=1000, D=64, n_planted=3, seed=66, chained=True, bf16=True),
+        sel=dict(mode="router", router_score="quest", router_mode="quantile", router_grain="row",
+                 router_quantile=0.25, budget_blocks=3, k_min=1, k_max=112), attn=True),
+    "v1_default_clamp": dict(
+        inp=dict(B=1, Hq=2, Hkv=2, S=1536, D=64, n_planted=4, seed=67, chained=False, bf16=False),
+        sel=dict(mode="router", router_score="mean", router_mode="quantile", router_grain="row",
+                 router_quantile=0.2, budget_blocks=2, k_min=8, k_max=112), attn=False),
+}
+
+
+def run_reference_v1(ref_src: str, name: str, spec: dict) -> dict:
+    """The reference's v1 selector (and reference_attn on its keep mask), with the
+    per-row scores it ranks, its margins and threshold, and its SEL.log records."""
+    import torch
+
+    if ref_src not in sys.path:
+        sys.path.insert(0, ref_src)
+    import sparse_attention as sa
+    from transformers.models.qwen2.modeling_qwen2 import repeat_kv
+    from triton_block_attn import reference_attn
+
+    inp, sel = spec["inp"], spec["sel"]
+    q, k, v, _ = planted_inputs(inp["B"], inp["Hq"], inp["Hkv"], inp["S"], inp["D"], n_planted=inp["n_planted"],
+                                seed=inp["seed"], chained=inp["chained"], bf16=inp["bf16"])
+    scale = inp["D"] ** -0.5
+    X = sa.SEL
+    X.kernel_v2 = False
+    for key in ("mode", "router_score", "router_mode", "router_grain", "router_quantile", "budget_blocks",
+                "k_min", "k_max"):
+        setattr(X, key, sel[key])
+    X.router_tau = sel.get("router_tau", 0.10)
+    X.log = True
+    X.reset_log()
+    g = inp["Hq"] // inp["Hkv"]
+    qt = torch.from_numpy(q)
+    kt = repeat_kv(torch.from_numpy(k), g)
+    captured = {}
+    orig_topk, orig_kth = torch.Tensor.topk, torch.Tensor.kthvalue
+
+    def topk_hook(self, *a, **kw):
+        captured.setdefault("row_score", self.detach().clone())   # the first topk ranks the raw scores
+        return orig_topk(self, *a, **kw)
+
+    def kth_hook(self, *a, **kw):
+        r = orig_kth(self, *a, **kw)
+        captured["m_safe"] = self.detach().clone()
+        captured["kquant"] = int(a[0] if a else kw["k"])
+        captured["thresh"] = float(r.values)
+        return r
+
+    torch.Tensor.topk, torch.Tensor.kthvalue = topk_hook, kth_hook
+    try:
+        keep = sa._block_select_mask(qt, kt, scale, 0)
+    finally:
+        torch.Tensor.topk, torch.Tensor.kthvalue = orig_topk, orig_kth
+    X.log = False
+    keep_np = keep.numpy().astype(bool)
+    # per-row scores and attention rows are stored for a few sampled tiles (size)
+    qt_n = math.ceil(inp["S"] / 64)
+    tiles = sorted({0, 3, qt_n // 2, qt_n - 1})
+    rows = np.concatenate([np.arange(t * 64, min(inp["S"], (t + 1) * 64)) for t in tiles])
+    out = {
+        "input_digest": input_digest(q, k, v),
+        "scale": np.float32(scale),
+        "meta": json.dumps({"name": name, "inp": inp, "sel": sel, "sample_tiles": tiles}),
+        "keep_ref": np.packbits(keep_np, axis=-1),
+        "nb": np.int64(keep_np.shape[-1]),
+        "sample_rows": rows.astype(np.int64),
+        "row_score_ref": captured["row_score"].numpy().astype(np.float32)[:, :, rows],
+        "kept_blocks_ref": np.stack([x.numpy() for x in X.kept_blocks.values()]),
+        "budget_samples_ref": np.array(X.budget_samples, np.float64),
+    }
+    if sel["mode"] == "router":
+        out["trigger_rate_ref"] = np.array(X.router_trigger_rate, np.float64)
+        out["eff_budget_ref"] = np.array(X.router_eff_budget, np.float64)
+        out["margin_mean_ref"] = np.array(X.router_margin_mean, np.float64)
+    if "m_safe" in captured:
+        out["m_safe_ref"] = captured["m_safe"].numpy().astype(np.float32)
+        out["kquant_ref"] = np.int64(captured["kquant"])
+        out["thresh_ref"] = np.float32(captured["thresh"])
+    if spec["attn"]:
+        vt = repeat_kv(torch.from_numpy(v), g)
+        out["attn_ref"] = reference_attn(qt, kt, vt, keep, scale).numpy().astype(np.float32)[:, :, rows]
+    return out
 
 
 def run_reference_config(ref_src: str, name: str, spec: dict) -> dict:
@@ -304,8 +419,19 @@ def main():
                     help="root of the reference project (its src/ is imported); or set UGBSA_REFERENCE")
     ap.add_argument("--only", default=None)
     ap.add_argument("--configs", action="store_true", help="record the BASELINE configurations (CONFIG_CASES)")
+    ap.add_argument("--v1", action="store_true", help="record the v1 per-row selector cases (V1_CASES)")
     args = ap.parse_args()
     ref_src = os.path.join(args.ref, "src")
+    if args.v1:
+        os.makedirs(os.path.join(HERE, "v1"), exist_ok=True)
+        for name, spec in V1_CASES.items():
+            if args.only and name != args.only:
+                continue
+            rec = run_reference_v1(ref_src, name, spec)
+            path = os.path.join(HERE, "v1", f"{name}.npz")
+            np.savez_compressed(path, **rec)
+            print(f"wrote {path} ({os.path.getsize(path)} bytes)")
+        return
     if args.configs:
         os.makedirs(os.path.join(HERE, "configs"), exist_ok=True)
         for name, spec in CONFIG_CASES.items():

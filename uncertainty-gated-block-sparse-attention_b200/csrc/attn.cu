@@ -75,6 +75,10 @@ struct AttnParams {
     // GPUs' buffers (NVLink stores; identical strides)
     void *dest[kMaxDest];
     int ndest;
+    // optional per-row keep mask [B, Hq, Sq, nbw] (the v1 per-row selector): a row
+    // uses a listed block only if its bit is set (triton_block_attn.py:87-104)
+    const uint32_t *rowmask;
+    int nbw;
 };
 
 __device__ __forceinline__ void tmem_ld16x256_x16(uint32_t taddr, uint32_t (&r)[64]) {
@@ -354,6 +358,24 @@ __global__ void __launch_bounds__(kAttnThreads, (D <= 128) ? 2 : 1)
 #pragma unroll
                 for (int e = 32; e < 64; ++e) x[e] = -INFINITY;
             }
+            if (p.rowmask) {
+                // rows of the tile that did not select a listed block: -inf there
+                const int64_t rbase = ((int64_t)b * p.Hq + h) * p.Sq + tile_row;
+                const int lr0 = r0, lr1 = r0 + 8;
+                const bool in0 = tile_row + lr0 < p.Sq, in1 = tile_row + lr1 < p.Sq;
+                const uint32_t *m0p = p.rowmask + (rbase + (in0 ? lr0 : 0)) * p.nbw;
+                const uint32_t *m1p = p.rowmask + (rbase + (in1 ? lr1 : 0)) * p.nbw;
+                const bool k00 = !in0 || ((__ldg(m0p + (blk0 >> 5)) >> (blk0 & 31)) & 1u);
+                const bool k10 = !in1 || ((__ldg(m1p + (blk0 >> 5)) >> (blk0 & 31)) & 1u);
+                const bool k01 = nb < 2 || !in0 || ((__ldg(m0p + (blk1 >> 5)) >> (blk1 & 31)) & 1u);
+                const bool k11 = nb < 2 || !in1 || ((__ldg(m1p + (blk1 >> 5)) >> (blk1 & 31)) & 1u);
+#pragma unroll
+                for (int c = 0; c < 16; ++c) {
+                    const bool keep0 = (c < 8) ? k00 : k01, keep1 = (c < 8) ? k10 : k11;
+                    if (!keep0) { x[4 * c] = -INFINITY; x[4 * c + 1] = -INFINITY; }
+                    if (!keep1) { x[4 * c + 2] = -INFINITY; x[4 * c + 3] = -INFINITY; }
+                }
+            }
             if (mask0 || mask1) {
 #pragma unroll
                 for (int c = 0; c < 16; ++c) {
@@ -574,7 +596,7 @@ template <int D, bool BF16>
 static int launch_attn_t(const void *Q, const void *K, const void *V, ugbsa_strides qs, ugbsa_strides ks,
                          ugbsa_strides vs, const int32_t *kv_idx, int kmax, int B, int Hq, int Hkv, int Sq, int Sk,
                          int t_base, int pair_stride, float scale, void *out, ugbsa_strides os, void *const *peers,
-                         int npeers, cudaStream_t stream, int *err) {
+                         int npeers, cudaStream_t stream, int *err, const uint32_t *rowmask = nullptr) {
     using L = AttnSmem<D>;
     CUtensorMap mQ, mK, mV;
     int rc;
@@ -596,6 +618,8 @@ static int launch_attn_t(const void *Q, const void *K, const void *V, ugbsa_stri
         p.row_limit = Sk;
     }
     p.NB = (Sk + 63) / 64;
+    p.rowmask = rowmask;
+    p.nbw = (p.NB + 31) / 32;
     p.scale_log2 = scale * 1.4426950408889634f;
     p.out = out;
     p.os_b = os.b; p.os_h = os.h; p.os_s = os.s;
@@ -638,6 +662,24 @@ int launch_attn(const void *Q, const void *K, const void *V, int dtype, ugbsa_st
                                             pair_stride, scale, out, os, peers, npeers, stream, err)               \
                   : launch_attn_t<DD, false>(Q, K, V, qs, ks, vs, kv_idx, kmax, B, Hq, Hkv, Sq, Sk, t_base,       \
                                              pair_stride, scale, out, os, peers, npeers, stream, err);
+    UGBSA_ATTN_CASE(64)
+    UGBSA_ATTN_CASE(128)
+    UGBSA_ATTN_CASE(256)
+#undef UGBSA_ATTN_CASE
+    return UGBSA_ERR_UNSUPPORTED;
+}
+
+int launch_attn_rowmask(const void *Q, const void *K, const void *V, int dtype, ugbsa_strides qs, ugbsa_strides ks,
+                        ugbsa_strides vs, const int32_t *kv_idx, int kmax, const uint32_t *rowmask, int B, int Hq,
+                        int Hkv, int Sq, int Sk, int D, float scale, void *out, ugbsa_strides os, cudaStream_t stream,
+                        int *err) {
+    const bool bf = (dtype == UGBSA_BF16);
+#define UGBSA_ATTN_CASE(DD)                                                                                        \
+    if (D == DD)                                                                                                   \
+        return bf ? launch_attn_t<DD, true>(Q, K, V, qs, ks, vs, kv_idx, kmax, B, Hq, Hkv, Sq, Sk, 0, 1, scale,   \
+                                            out, os, nullptr, 0, stream, err, rowmask)                            \
+                  : launch_attn_t<DD, false>(Q, K, V, qs, ks, vs, kv_idx, kmax, B, Hq, Hkv, Sq, Sk, 0, 1, scale,  \
+                                             out, os, nullptr, 0, stream, err, rowmask);
     UGBSA_ATTN_CASE(64)
     UGBSA_ATTN_CASE(128)
     UGBSA_ATTN_CASE(256)

@@ -545,3 +545,59 @@ int ugbsa_read_device_error(ugbsa_stream_t stream, int *bits) {
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------ v1 per-row selection
+size_t ugbsa_select_rows_workspace_bytes(const ugbsa_selector_config *cfg, int B, int Hq, int S) {
+    (void)cfg;
+    if (B <= 0 || Hq <= 0 || S <= 0) return 0;
+    return select_rows_workspace_bytes(B, Hq, S);
+}
+
+int ugbsa_select_rows(const void *Q, int dtype, ugbsa_strides qs, const float *summ_a, const float *summ_b, int B,
+                      int Hq, int Hkv, int S, int D, float scale, const ugbsa_selector_config *cfg,
+                      uint32_t *keep_bits, int32_t *kv_idx, float *sigma, uint8_t *trigger, void *workspace,
+                      size_t workspace_bytes, ugbsa_stream_t stream) {
+    int rc = check_cfg(cfg);
+    if (rc) return rc;
+    if (B <= 0 || Hq <= 0 || Hkv <= 0 || S <= 0 || D <= 0 || Hq % Hkv) return UGBSA_ERR_SHAPE;
+    if (D % 8 || D > 256) return UGBSA_ERR_UNSUPPORTED;
+    if (dtype < UGBSA_F32 || dtype > UGBSA_F16) return UGBSA_ERR_DTYPE;
+    if ((rc = check_view(Q, dtype, qs))) return rc;
+    if (!summ_a || (cfg_is_quest(cfg) && !summ_b) || !keep_bits) return UGBSA_ERR_ARG;
+    if (!aligned16(summ_a) || (cfg_is_quest(cfg) && !aligned16(summ_b))) return UGBSA_ERR_ALIGN;
+    const int NB = (S + 63) / 64;
+    if (NB > 6144) return UGBSA_ERR_SHAPE;   // a row's block keys are ranked in shared memory
+    if (!workspace || workspace_bytes < select_rows_workspace_bytes(B, Hq, S)) return UGBSA_ERR_WORKSPACE;
+    if (!aligned16(workspace)) return UGBSA_ERR_ALIGN;
+    return launch_select_rows(Q, dtype, qs, summ_a, summ_b, B, Hq, Hkv, S, D, scale, cfg, keep_bits, kv_idx, sigma,
+                              trigger, workspace, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int ugbsa_keep_to_tiles(const uint8_t *keep, uint32_t *keep_bits, int B, int H, int S, int32_t *kv_idx,
+                        ugbsa_stream_t stream) {
+    if (B <= 0 || H <= 0 || S <= 0) return UGBSA_ERR_SHAPE;
+    if (!keep_bits) return UGBSA_ERR_ARG;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    int rc;
+    if (keep && (rc = launch_keep_pack(keep, B, H, S, (S + 63) / 64, keep_bits, st))) return rc;
+    if (kv_idx) return launch_rows_to_tiles(keep_bits, B, H, S, kv_idx, st);
+    return UGBSA_OK;
+}
+
+int ugbsa_attn_rowmask(const void *Q, const void *K, const void *V, int dtype, ugbsa_strides qs, ugbsa_strides ks,
+                       ugbsa_strides vs, const int32_t *kv_idx, int kmax, const uint32_t *keep_bits, int B, int Hq,
+                       int Hkv, int S, int D, float scale, void *out, ugbsa_strides os, ugbsa_stream_t stream) {
+    if (B <= 0 || Hq <= 0 || Hkv <= 0 || S <= 0 || Hq % Hkv || kmax <= 0) return UGBSA_ERR_SHAPE;
+    if (D != 64 && D != 128 && D != 256) return UGBSA_ERR_UNSUPPORTED;
+    if (dtype != UGBSA_BF16 && dtype != UGBSA_F16) return UGBSA_ERR_DTYPE;
+    int rc;
+    if ((rc = check_view(Q, dtype, qs)) || (rc = check_view(K, dtype, ks)) || (rc = check_view(V, dtype, vs)) ||
+        (rc = check_view(out, dtype, os)))
+        return rc;
+    if (!kv_idx || !keep_bits) return UGBSA_ERR_ARG;
+    if (kmax > 8192) return UGBSA_ERR_SHAPE;
+    int *err = device_error_word();
+    if (!err) return UGBSA_ERR_NO_DEVICE;
+    return launch_attn_rowmask(Q, K, V, dtype, qs, ks, vs, kv_idx, kmax, keep_bits, B, Hq, Hkv, S, S, D, scale, out,
+                               os, reinterpret_cast<cudaStream_t>(stream), err);
+}

@@ -41,6 +41,8 @@ struct SelParams {
     // order statistics (the STATS variant): ranks k_b and rho_k of the unforced sort
     int k_b, rho_k;
     float *st_g, *st_r, *st_sigma, *st_grho;   // [B*Hq*Qt] each
+    // per-row scores (the ROWS variant, the v1 selector): [B,Hq,S,NB], blocks < the tile's nvis
+    float *row_scores;
 };
 
 __device__ __forceinline__ void load8f(const float *p, float (&x)[8]) {
@@ -84,7 +86,9 @@ struct SelLayout {
 
 // STATS: instead of kv_idx / sigma, the order statistics of the block-score
 // diagnostic over the unforced, causally masked tile scores (p.st_*).
-template <typename T, bool QUEST, int NBC, int TB, bool STATS = false>
+// ROWS: every row's score of every block up to the tile's last visible one goes
+// to p.row_scores (the v1 selector ranks blocks per row); no tile max, no ranking.
+template <typename T, bool QUEST, int NBC, int TB, bool STATS = false, bool ROWS = false>
 __global__ void __launch_bounds__(kSelThreads) select_tile_kernel(const T *__restrict__ Q, int64_t qb, int64_t qh,
                                                                    int64_t qs, const float *__restrict__ summ_a,
                                                                    const float *__restrict__ summ_b,
@@ -200,6 +204,22 @@ __global__ void __launch_bounds__(kSelThreads) select_tile_kernel(const T *__res
                 }
             }
         }
+        if constexpr (ROWS) {
+            float *rs = p.row_scores + (((int64_t)b * p.Hq + h) * p.S) * p.NB;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int row = t * 64 + 4 * ty + i;
+                if (row >= p.S) continue;
+#pragma unroll
+                for (int j = 0; j < TB; ++j) {
+                    const int blk = c0 + TB * tx + j;
+                    if (blk >= nvis) continue;
+                    rs[(int64_t)row * p.NB + blk] = QUEST ? __fmul_rn(__fadd_rn(acc[i][j], acc2[i][j]), p.scale)
+                                                          : __fmul_rn(acc[i][j], p.scale);
+                }
+            }
+            continue;
+        }
         // scores -> max over this thread's 4 rows
         float m[TB];
 #pragma unroll
@@ -230,6 +250,7 @@ __global__ void __launch_bounds__(kSelThreads) select_tile_kernel(const T *__res
             if (c0 + tid < nvis) ts[c0 + tid] = v;
         }
     }
+    if constexpr (ROWS) return;
     __syncthreads();
 
     // ---- ranking keys: descending score, ties -> lower block id
@@ -571,14 +592,14 @@ static int next_pow2(int x) {
     return p;
 }
 
-template <typename T, bool QUEST, int NBC, int TB, bool STATS = false>
+template <typename T, bool QUEST, int NBC, int TB, bool STATS = false, bool ROWS = false>
 static int launch_tile_t(const T *Q, ugbsa_strides qs, const float *sa, const float *sb, const SelParams &sp,
                          cudaStream_t stream) {
     using L = SelLayout<NBC>;
     const size_t smem = (size_t)sp.D * L::QSTR * 4 + (size_t)sp.D * L::KSTR * 4 * (QUEST ? 2 : 1) +
-                        (size_t)8 * NBC * 4 + (size_t)sp.NBpad * 4 + (size_t)sp.NBpad * 8 + 16;
+                        (ROWS ? (size_t)16 : (size_t)8 * NBC * 4 + (size_t)sp.NBpad * 4 + (size_t)sp.NBpad * 8 + 16);
     if (smem > 227 * 1024) return UGBSA_ERR_SHAPE;
-    auto kern = select_tile_kernel<T, QUEST, NBC, TB, STATS>;
+    auto kern = select_tile_kernel<T, QUEST, NBC, TB, STATS, ROWS>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return UGBSA_ERR_LAUNCH;
     const int64_t grid = (int64_t)sp.B * sp.Hq * sp.Qt;
@@ -587,15 +608,35 @@ static int launch_tile_t(const T *Q, ugbsa_strides qs, const float *sa, const fl
     return cudaGetLastError() == cudaSuccess ? UGBSA_OK : UGBSA_ERR_LAUNCH;
 }
 
-template <typename T, bool STATS = false>
+template <typename T, bool STATS = false, bool ROWS = false>
 static int launch_tile_d(const T *Q, ugbsa_strides qs, const float *sa, const float *sb, bool quest,
                          const SelParams &sp, cudaStream_t stream) {
     if (sp.D <= 128) {
-        return quest ? launch_tile_t<T, true, 64, 4, STATS>(Q, qs, sa, sb, sp, stream)
-                     : launch_tile_t<T, false, 64, 4, STATS>(Q, qs, sa, sb, sp, stream);
+        return quest ? launch_tile_t<T, true, 64, 4, STATS, ROWS>(Q, qs, sa, sb, sp, stream)
+                     : launch_tile_t<T, false, 64, 4, STATS, ROWS>(Q, qs, sa, sb, sp, stream);
     }
-    return quest ? launch_tile_t<T, true, 32, 2, STATS>(Q, qs, sa, sb, sp, stream)
-                 : launch_tile_t<T, false, 32, 2, STATS>(Q, qs, sa, sb, sp, stream);
+    return quest ? launch_tile_t<T, true, 32, 2, STATS, ROWS>(Q, qs, sa, sb, sp, stream)
+                 : launch_tile_t<T, false, 32, 2, STATS, ROWS>(Q, qs, sa, sb, sp, stream);
+}
+
+// per-row scores [B,Hq,S,NB] of every (row, block up to the row's tile) -- the v1 selector's input
+int launch_row_scores(const void *Q, int dtype, ugbsa_strides qs, const float *summ_a, const float *summ_b, int B,
+                      int Hq, int Hkv, int S, int D, float scale, bool quest, float *row_scores,
+                      cudaStream_t stream) {
+    const int NB = (S + 63) / 64;
+    SelParams sp{};
+    sp.B = B; sp.Hq = Hq; sp.Hkv = Hkv; sp.S = S; sp.D = D; sp.NB = NB; sp.Qt = NB;
+    sp.NBpad = next_pow2(NB);
+    sp.scale = scale;
+    sp.row_scores = row_scores;
+    switch (dtype) {
+        case UGBSA_F32: return launch_tile_d<float, false, true>((const float *)Q, qs, summ_a, summ_b, quest, sp, stream);
+        case UGBSA_BF16:
+            return launch_tile_d<__nv_bfloat16, false, true>((const __nv_bfloat16 *)Q, qs, summ_a, summ_b, quest, sp,
+                                                             stream);
+        case UGBSA_F16: return launch_tile_d<__half, false, true>((const __half *)Q, qs, summ_a, summ_b, quest, sp, stream);
+    }
+    return UGBSA_ERR_DTYPE;
 }
 
 static bool cfg_quest(const ugbsa_selector_config *cfg) {

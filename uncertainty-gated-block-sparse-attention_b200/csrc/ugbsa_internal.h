@@ -99,6 +99,22 @@ int launch_attn(const void *Q, const void *K, const void *V, int dtype, ugbsa_st
                 ugbsa_strides vs, const int32_t *kv_idx, int kmax, int B, int Hq, int Hkv, int Sq, int Sk, int D,
                 int t_base, int pair_stride, float scale, void *out, ugbsa_strides os, void *const *peers,
                 int npeers, cudaStream_t stream, int *err);
+// v1 per-row selector (select_rows.cu); row scores by select_tile_kernel<..., ROWS> (select.cu)
+int launch_row_scores(const void *Q, int dtype, ugbsa_strides qs, const float *summ_a, const float *summ_b, int B,
+                      int Hq, int Hkv, int S, int D, float scale, bool quest, float *row_scores, cudaStream_t stream);
+size_t select_rows_workspace_bytes(int B, int Hq, int S);
+void rows_budget(const ugbsa_selector_config *cfg, int NB, int *k_bud, int *k_eff);
+int launch_select_rows(const void *Q, int dtype, ugbsa_strides qs, const float *summ_a, const float *summ_b, int B,
+                       int Hq, int Hkv, int S, int D, float scale, const ugbsa_selector_config *cfg,
+                       uint32_t *keep_bits, int32_t *kv_idx, float *sigma_out, uint8_t *trigger_out, void *workspace,
+                       cudaStream_t stream);
+int launch_rows_to_tiles(const uint32_t *keep_bits, int B, int H, int S, int32_t *kv_idx, cudaStream_t stream);
+int launch_keep_pack(const uint8_t *keep, int B, int H, int S, int NB, uint32_t *bits, cudaStream_t stream);
+// attention with a per-row keep mask [B, Hq, Sq, ceil(NB/32)] (launch_attn's kernels, whole sequence)
+int launch_attn_rowmask(const void *Q, const void *K, const void *V, int dtype, ugbsa_strides qs, ugbsa_strides ks,
+                        ugbsa_strides vs, const int32_t *kv_idx, int kmax, const uint32_t *rowmask, int B, int Hq,
+                        int Hkv, int Sq, int Sk, int D, float scale, void *out, ugbsa_strides os, cudaStream_t stream,
+                        int *err);
 // fp32 Q/K/V (CUDA cores, attn_f32.cu); same row mapping as launch_attn, no peers
 int launch_attn_f32(const float *Q, const float *K, const float *V, ugbsa_strides qs, ugbsa_strides ks,
                     ugbsa_strides vs, const int32_t *kv_idx, int kmax, int B, int Hq, int Hkv, int Sq, int Sk, int D,

@@ -86,6 +86,12 @@ SIGNATURES = {
                               P, ctypes.c_size_t, P]),
     "ugbsa_qk_norm_rope": (I, [P, I, Strides, P, I, ctypes.c_float, P, P, ctypes.c_int64, ctypes.c_int64, I, I, I,
                                I, I, P, Strides, I, P, P, P]),
+    "ugbsa_select_rows_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(SelectorConfig), I, I, I]),
+    "ugbsa_select_rows": (I, [P, I, Strides, P, P, I, I, I, I, I, ctypes.c_float, ctypes.POINTER(SelectorConfig),
+                              P, P, P, P, P, ctypes.c_size_t, P]),
+    "ugbsa_keep_to_tiles": (I, [P, P, I, I, I, P, P]),
+    "ugbsa_attn_rowmask": (I, [P, P, P, I, Strides, Strides, Strides, P, I, P, I, I, I, I, I, ctypes.c_float, P,
+                               Strides, P]),
     "ugbsa_block_order_stats_workspace_bytes": (ctypes.c_size_t, [I, I, I]),
     "ugbsa_block_order_stats": (I, [P, I, Strides, P, P, I, I, I, I, I, ctypes.c_float, I, I, P, P, P, P, P, P,
                                     ctypes.c_size_t, P]),

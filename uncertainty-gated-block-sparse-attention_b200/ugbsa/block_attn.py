@@ -2,7 +2,8 @@
 
 ``block_sparse_attn_v2`` keeps the reference's signature
 (src/triton_block_attn.py:267-298) and runs libugbsa's sm_100a tcgen05 kernel
-instead of Triton.  K/V may carry fewer heads than Q (GQA, Hq % Hkv == 0); the
+instead of Triton; ``block_sparse_attn`` is the v1 launcher (:150-181) with a
+per-row keep mask, on the same kernel with its row mask.  K/V may carry fewer heads than Q (GQA, Hq % Hkv == 0); the
 reference requires equal shapes after repeat_kv (:276), which still works.
 
 ``reference_attn`` is the reference's masked-SDPA checker (:301-312): a plain
@@ -24,6 +25,17 @@ def block_sparse_attn_v2(q, k, v, kv_idx, scale, block_n=64, block_m=64, num_war
     if block_n != 64 or block_m != 64:
         raise ValueError("block_n and block_m are fixed at 64")
     return ops.block_sparse_attn(q, k, v, kv_idx, float(scale))
+
+
+def block_sparse_attn(q, k, v, keep, scale, block_n=64, block_m=64, num_warps=4, num_stages=1):
+    """The reference's v1 launcher (src/triton_block_attn.py:150-181): keep
+    [B,H,M,NB] bool per query row; each tile attends to the union of its rows'
+    blocks with every row masked to its own (triton_block_attn.py:87-104).
+    q [B,H,M,D], k/v [B,Hkv,M,D] bf16 / fp16 CUDA.  Returns [B,H,M,D]."""
+    if block_n != 64 or block_m != 64:
+        raise ValueError("block_n and block_m are fixed at 64")
+    bits, kv_idx = ops.keep_to_tiles(keep)
+    return ops.block_sparse_attn_rows(q, k, v, kv_idx, bits, float(scale))
 
 
 def reference_attn(q, k, v, keep, scale, block_n=64):

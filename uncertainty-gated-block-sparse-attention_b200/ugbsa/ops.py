@@ -196,6 +196,84 @@ def block_sparse_attn(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kv_idx:
     return out
 
 
+# ------------------------------------------------------------------ v1 per-row selection
+def select_rows(query: torch.Tensor, key: torch.Tensor, scaling: float, cfg: SelectorConfig,
+                return_router: bool = False, summ=None, with_tiles: bool = True):
+    """The v1 per-row selector (ugbsa_select_rows): keep bits [B,Hq,S,ceil(NB/32)]
+    int32 (bit j of a row: block j kept) and, with ``with_tiles``, each tile's
+    union list kv_idx [B,Hq,Qt,NB] (ascending, sentinel NB); with
+    ``return_router`` also the margins after the grain step [B,Hq,S] (+inf for
+    ineligible rows) and the triggers.  ``key`` may carry Hkv or Hq heads."""
+    _need_cuda(query, key)
+    B, Hq, S, D = query.shape
+    if key.shape[0] != B or key.shape[2] != S or key.shape[3] != D or Hq % key.shape[1]:
+        raise ValueError(f"incompatible query {tuple(query.shape)} / key {tuple(key.shape)}")
+    query = _inner_contig(query)
+    if summ is None:
+        summ = block_summary(key, cfg.quest)
+    sa, sb = (summ if cfg.quest else (summ, None))
+    nb = math.ceil(S / BLOCK)
+    nbw = (nb + 31) // 32
+    bits = torch.empty((B, Hq, S, nbw), device=query.device, dtype=torch.int32)
+    kv_idx = torch.empty((B, Hq, nb, nb), device=query.device, dtype=torch.int32) if with_tiles else None
+    sigma = torch.empty((B, Hq, S), device=query.device, dtype=torch.float32) if return_router else None
+    trig = torch.empty((B, Hq, S), device=query.device, dtype=torch.uint8) if return_router else None
+    c = cfg.to_c()
+    L = _lib.load()
+    ws_bytes = L.ugbsa_select_rows_workspace_bytes(ctypes.byref(c), B, Hq, S)
+    ws = torch.empty((ws_bytes,), device=query.device, dtype=torch.uint8)
+    rc = L.ugbsa_select_rows(_ptr(query), _DTYPES[query.dtype], _strides(query), _ptr(sa), _ptr(sb), B, Hq,
+                             key.shape[1], S, D, ctypes.c_float(scaling), ctypes.byref(c), _ptr(bits), _ptr(kv_idx),
+                             _ptr(sigma), _ptr(trig), _ptr(ws), ctypes.c_size_t(ws_bytes), _stream())
+    _lib.check(rc, "ugbsa_select_rows")
+    if return_router:
+        return bits, kv_idx, sigma, trig.bool()
+    return bits, kv_idx
+
+
+def keep_to_tiles(keep: torch.Tensor):
+    """A keep mask [B,H,S,NB] (bool / uint8) -> (bits [B,H,S,ceil(NB/32)] int32,
+    kv_idx [B,H,Qt,NB]: each tile's union of its rows' blocks, ascending)."""
+    _need_cuda(keep)
+    B, H, S, nb = keep.shape
+    if nb != math.ceil(S / BLOCK):
+        raise ValueError(f"keep must be [B,H,S,ceil(S/64)], got {tuple(keep.shape)}")
+    k8 = keep.to(torch.uint8).contiguous()
+    bits = torch.empty((B, H, S, (nb + 31) // 32), device=keep.device, dtype=torch.int32)
+    kv_idx = torch.empty((B, H, nb, nb), device=keep.device, dtype=torch.int32)
+    rc = _lib.load().ugbsa_keep_to_tiles(_ptr(k8), _ptr(bits), B, H, S, _ptr(kv_idx), _stream())
+    _lib.check(rc, "ugbsa_keep_to_tiles")
+    return bits, kv_idx
+
+
+def unpack_keep(bits: torch.Tensor, nb: int) -> torch.Tensor:
+    """keep bits [..., ceil(NB/32)] -> bool [..., NB] (device ops)."""
+    shifts = torch.arange(32, device=bits.device, dtype=torch.int32)
+    b = (bits.unsqueeze(-1) >> shifts) & 1
+    return b.reshape(*bits.shape[:-1], -1)[..., :nb].bool()
+
+
+def block_sparse_attn_rows(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kv_idx: torch.Tensor,
+                           keep_bits: torch.Tensor, scale: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Attention over the tiles' union lists with the per-row keep mask
+    (ugbsa_attn_rowmask): q [B,Hq,S,D], k/v [B,Hkv,S,D] bf16 / fp16."""
+    _need_cuda(q, k, v, kv_idx, keep_bits)
+    if q.dtype not in (torch.bfloat16, torch.float16) or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise ValueError("the per-row masked attention takes bf16 or fp16 q/k/v of one dtype")
+    B, Hq, S, D = q.shape
+    Hkv = k.shape[1]
+    q, k, v = _inner_contig(q), _inner_contig(k), _inner_contig(v)
+    if out is None:
+        out = torch.empty((B, Hq, S, D), device=q.device, dtype=q.dtype)
+    kv_idx = kv_idx.contiguous()
+    keep_bits = keep_bits.contiguous()
+    rc = _lib.load().ugbsa_attn_rowmask(_ptr(q), _ptr(k), _ptr(v), _DTYPES[q.dtype], _strides(q), _strides(k),
+                                        _strides(v), _ptr(kv_idx), kv_idx.shape[-1], _ptr(keep_bits), B, Hq, Hkv,
+                                        S, D, ctypes.c_float(scale), _ptr(out), _strides(out), _stream())
+    _lib.check(rc, "ugbsa_attn_rowmask")
+    return out
+
+
 def slice_rows(S: int, row_base: int, pair_stride: int, n_tiles: int) -> int:
     """Query rows of a slice of n_tiles local tiles (see ugbsa_select_tiles_rows):
     local tile t is sequence tile row_base/64 + t + 2*(t//2)*(pair_stride-1)."""

@@ -20,13 +20,13 @@ The hook looks up ``_block_select_kv_idx_v2`` through this module's globals
 at call time, so a diagnostics wrapper can monkey-patch it the way the
 reference's dump hook does (src/dump_block_scores.py:64-69).
 
-Scope: the v2 modes topk / quest / router with ``kernel_v2=True``, plus the
-dense / decode path through SDPA.  ``SEL.decode_sparse = True`` (an addition,
+Scope: the modes topk / quest / router, per tile (``kernel_v2=True``, the v2
+path) or per query row (``kernel_v2=False``, the v1 path with its per-row
+inner mask: ``_block_select_mask``), plus the dense / decode path through SDPA.  ``SEL.decode_sparse = True`` (an addition,
 off by default) sends decode calls (Q == 1) through the block-sparse decode
 instead: the v2 policy on the decode row over the cache's block summaries
-(``SUMM_CACHE``, refreshed incrementally per layer).  The v1 research policies (belief, rollout,
-rollout_peek, per-row keep masks) are outside this build and raise
-``NotImplementedError``.
+(``SUMM_CACHE``, refreshed incrementally per layer).  The research policies (belief, rollout,
+rollout_peek) are outside this build and raise ``NotImplementedError``.
 """
 from __future__ import annotations
 
@@ -150,6 +150,40 @@ def _block_select_kv_idx_v2(query, key_states, scaling, block_m=64):
     return kv_idx
 
 
+def _select_rows(query, key_states, scaling, layer_idx=0):
+    """v1 per-row selection on the device: (keep bits, the tiles' union lists).
+    Fills the SEL.log records as the reference's v1 selector does
+    (src/sparse_attention.py:350-382)."""
+    cfg = SEL.config()
+    router = cfg.mode == "router"
+    if SEL.log and router:
+        bits, kv_idx, sigma, trig = ops.select_rows(query, key_states, float(scaling), cfg, return_router=True)
+    else:
+        bits, kv_idx = ops.select_rows(query, key_states, float(scaling), cfg)
+    if SEL.log:
+        nb = math.ceil(key_states.shape[-2] / BLOCK)
+        last = ops.unpack_keep(bits[0, :, -1], nb)                       # [H, NB] of the last query row
+        if router:
+            keep_all = ops.unpack_keep(bits, nb)
+            SEL.router_trigger_rate.append(float(trig.float().mean().item()))
+            SEL.router_eff_budget.append(float(keep_all.float().sum(dim=-1).mean().item()))
+            # the mean of the raw per-(head, row) margins: rows with at most k_eff visible
+            # blocks (always the first ones) make it NaN, as in the reference
+            SEL.router_margin_mean.append(float("nan"))
+        SEL.kept_blocks[layer_idx] = last.any(dim=0).cpu()
+        SEL.budget_samples.append(float(last.sum(dim=-1).float().mean().item()))
+    return bits, kv_idx
+
+
+def _block_select_mask(query, key_states, scaling, layer_idx):
+    """The v1 per-row policy (src/sparse_attention.py:208-382, modes topk /
+    quest / router): bool keep [B, H, Q, n_blocks] -- each query row's own top
+    blocks (ties to the lower id), the sink and its own block, the router's
+    triggered rows dense.  Scores are fp32 whatever the input dtype."""
+    bits, _ = _select_rows(query, key_states, scaling, layer_idx)
+    return ops.unpack_keep(bits, math.ceil(key_states.shape[-2] / BLOCK))
+
+
 class SummaryCache:
     """Block summaries of each layer's growing KV cache, for the sparse decode:
     the first decode call of a layer summarises the whole cache, later calls
@@ -217,9 +251,16 @@ def block_sparse_attention(module, query, key, value, attention_mask, scaling, d
         ops.block_sparse_attn(query, key, value, kv_idx, float(scaling), out=out.transpose(1, 2))
         PROF.stop(ev)
         return out, None
+    if SEL.mode in ("topk", "router", "quest"):
+        # v1 path (:790-803): per-row selection, the tile's union list, per-row inner mask
+        B, H, S, D = query.shape
+        bits, kv_idx = _select_rows(query, key, scaling, getattr(module, "layer_idx", 0))
+        out = torch.empty((B, S, H, D), device=query.device, dtype=query.dtype)
+        ops.block_sparse_attn_rows(query, key, value, kv_idx, bits, float(scaling), out=out.transpose(1, 2))
+        return out, None
     raise NotImplementedError(
-        f"SEL.mode={SEL.mode!r} with kernel_v2={SEL.kernel_v2}: only the v2 modes "
-        "topk / quest / router (kernel_v2=True) and dense are built on B200")
+        f"SEL.mode={SEL.mode!r}: the research policies belief / rollout / rollout_peek are not built on B200; "
+        "topk / quest / router (v1 per-row or v2 per-tile) and dense are")
 
 
 def register():
