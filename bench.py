@@ -401,11 +401,18 @@ def run_gpu(args, seq):
         ts = torch.tensor([e2e["serial_ms"]], device=dev, dtype=torch.float64)
         if world > 1:
             dist.all_reduce(ts, op=dist.ReduceOp.MAX)
+        tc = torch.tensor([e2e.get("copy_only_ms", float("nan"))], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(tc, op=dist.ReduceOp.MAX)
+        copy_ms = tc.item()
         e2e = {"value": round(deq / (e2e_ms / 1e3) / 1e12, 3), "unit": UNIT,
                "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],   # over all ranks
                "ms_per_step": round(e2e_ms, 3),
                "pipelined": "copy-in of step i+1 and copy-out of step i-1 overlap step i (three streams)",
-               "serial_ms_per_step": round(ts.item(), 3)}
+               "serial_ms_per_step": round(ts.item(), 3),
+               # the same host<->device copies with no compute: the host-link ceiling of this e2e
+               "copy_only_ms_per_step": round(copy_ms, 3),
+               "frac_of_copy_ceiling": round(copy_ms / e2e_ms, 4) if e2e_ms > 0 else None}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:

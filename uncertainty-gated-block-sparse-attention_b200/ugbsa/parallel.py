@@ -392,6 +392,8 @@ class ShardedPrefill(_PeerOutput):
             return self.step(d[0], d[1], d[2], gather=False)
 
         t = pipelined_e2e([hq, hk, hv], compute, out_shape, q.dtype, steps, warmup)
+        c = pipelined_e2e([hq, hk, hv], lambda d: torch.empty(out_shape, device=q.device, dtype=q.dtype),
+                          out_shape, q.dtype, steps, warmup)
         per_head = B * S * D * q.element_size()
         if self.shard.world == 1:
             h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv))
@@ -399,7 +401,7 @@ class ShardedPrefill(_PeerOutput):
         else:
             h2d = self._qkv_heads * per_head
             d2h = self.shard.Hq * per_head
-        return {"ms": t["ms"], "serial_ms": t["serial_ms"], "h2d": h2d, "d2h": d2h}
+        return {"ms": t["ms"], "serial_ms": t["serial_ms"], "h2d": h2d, "d2h": d2h, "copy_only_ms": c["ms"]}
 
     def close(self):
         """Collective when peer output was used (releases the peer buffers)."""
@@ -710,6 +712,16 @@ class GridShardedPrefill(_PeerOutput):
         self._cell_counts = [(s.kv1 - s.kv0) * G * len(s.tiles(S)) for s in shards]
         self._nb = nb
         self._tiles_dev = None
+        # the m ranks that share a KV group (for the end-to-end path: each copies 1/m of
+        # the group's K / V rows from the host and the group all-gathers them over NVLink);
+        # every rank creates every group, in the same order
+        self._kv_group = None
+        if shard.world > 1 and shard.m > 1 and group is not None:
+            import torch.distributed as dist
+            for g in range(shard.world // shard.m):
+                pg = dist.new_group(list(range(g * shard.m, (g + 1) * shard.m)))
+                if g == shard.rank // shard.m:
+                    self._kv_group = pg
 
     def exchange_margins(self, cells: torch.Tensor, rowsum):
         import torch.distributed as dist
@@ -768,26 +780,72 @@ class GridShardedPrefill(_PeerOutput):
             events[2].record()
         return out.transpose(1, 2) if self.shard.world == 1 else out
 
+    def _split_kv(self, S: int) -> bool:
+        return self._kv_group is not None and S % self.shard.m == 0
+
+    def gather_kv_rows(self, k_part, v_part):
+        """K / V row blocks of this rank's KV heads (rows j*S/m .. (j+1)*S/m - 1 on rank j
+        of the group) -> the whole sequence on every rank of the group (NCCL all-gather
+        over NVLink)."""
+        import torch.distributed as dist
+        m = self.shard.m
+        outs = []
+        for x in (k_part, v_part):
+            B, hk, r, D = x.shape
+            full = torch.empty((m * B * hk, r, D), device=x.device, dtype=x.dtype)
+            dist.all_gather_into_tensor(full, x.reshape(B * hk, r, D).contiguous(), group=self._kv_group)
+            full = full.view(m, B, hk, r, D).permute(1, 2, 0, 3, 4).reshape(B, hk, m * r, D)
+            outs.append(full)
+        return outs
+
     def time_e2e(self, q, k, v, steps: int, warmup: int = 2):
-        """End to end: this rank's Q rows and its KV heads copied from pinned host
-        memory every step, its output rows read back (the layer output stays
-        sharded, as for a row-parallel output projection); serial and pipelined
-        (pipelined_e2e).  Byte counts are over all ranks."""
-        hq, hk, hv = (x.contiguous().cpu().pin_memory() for x in (q, k, v))
+        """End to end through the runner's public step(): every step this rank copies
+        from pinned host memory its Q rows and its share of its KV heads' rows (with m
+        ranks per KV group each copies 1/m of the group's K / V and the group
+        all-gathers them over NVLink, so every K / V byte crosses PCIe once), runs the
+        layer with the output gathered on every rank (gather=True), and reads back its
+        1/world slice of the [B, S, Hq, D] output rows (the job reads the output once).
+        Serial and pipelined (pipelined_e2e), plus the copy-only time of the same bytes
+        (the host-link ceiling).  Byte counts are over all ranks."""
+        sh = self.shard
+        world = sh.world
+        split = self._split_kv(self.S)
+        hq = q.contiguous().cpu().pin_memory()
+        if split:
+            r = self.S // sh.m
+            hk = k[:, :, sh.j * r:(sh.j + 1) * r].contiguous().cpu().pin_memory()
+            hv = v[:, :, sh.j * r:(sh.j + 1) * r].contiguous().cpu().pin_memory()
+        else:
+            hk, hv = (x.contiguous().cpu().pin_memory() for x in (k, v))
         B, hl, rows, D = q.shape
+        # this rank's slice of the gathered output: rows world-split
+        r0 = (self.S * sh.rank) // world
+        r1 = (self.S * (sh.rank + 1)) // world
         ridx = self.shard.rows(self.S).to(q.device) if self.shard.m > 1 else None
 
         def compute(d):
-            out = self.step(d[0], d[1], d[2], gather=False)
+            kk, vv = self.gather_kv_rows(d[1], d[2]) if split else (d[1], d[2])
+            if world > 1 and self.peer_output:
+                out = self.step(d[0], kk, vv, gather=True)         # [B, S, Hq, D] on every rank
+                # a copy: the gathered buffer is rewritten by the next step (ours and the peers')
+                return out[:, r0:r1].clone()
+            out = self.step(d[0], kk, vv, gather=False)
             return out.index_select(2, ridx) if ridx is not None else out
 
-        t = pipelined_e2e([hq, hk, hv], compute, (B, hl, rows, D), q.dtype, steps, warmup)
-        sh = self.shard
+        if world > 1 and self.peer_output:
+            out_shape, out_numel = (B, r1 - r0, sh.Hq, D), B * (r1 - r0) * sh.Hq * D
+        else:
+            out_shape, out_numel = (B, hl, rows, D), B * hl * rows * D
+        t = pipelined_e2e([hq, hk, hv], compute, out_shape, q.dtype, steps, warmup)
+        c = pipelined_e2e([hq, hk, hv], lambda d: torch.empty(out_shape, device=q.device, dtype=q.dtype),
+                          out_shape, q.dtype, steps, warmup)
         el = q.element_size()
         per_head_rows = B * self.S * D * el
-        # every rank copies its Q rows (all Q once over the job) and its KV heads (m copies of each)
-        h2d = sh.Hq * per_head_rows + 2 * sh.Hkv * sh.m * per_head_rows
-        return {"ms": t["ms"], "serial_ms": t["serial_ms"], "h2d": h2d, "d2h": sh.Hq * per_head_rows}
+        kv_copies = 1 if split else sh.m
+        h2d = sh.Hq * per_head_rows + 2 * sh.Hkv * kv_copies * per_head_rows
+        d2h = sh.Hq * per_head_rows if (world > 1 and self.peer_output) else sh.Hq * per_head_rows
+        return {"ms": t["ms"], "serial_ms": t["serial_ms"], "h2d": h2d, "d2h": d2h,
+                "copy_only_ms": c["ms"], "rank_bytes": sum(x.numel() * el for x in (hq, hk, hv)) + out_numel * el}
 
     def close(self):
         """Collective when peer output was used (releases the peer buffers)."""
