@@ -322,10 +322,12 @@ def run_gpu(args, seq):
     sampler = ClockSampler(dev.index if "CUDA_VISIBLE_DEVICES" not in os.environ else
                            os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local])
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
-    barrier()
-    torch.cuda.synchronize()
+    # the clock sampler first, then the barrier: every rank records its start event
+    # right after the same collective (a skewed start would be counted as step time)
     sampler.start()
     time.sleep(0.25)
+    barrier()
+    torch.cuda.synchronize()
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
     t_start.record(stream)
