@@ -129,6 +129,7 @@ class TPDecoder:
         self.layout = TPLayout.make(shape, world, rank)
         self.scale = shape.head_dim ** -0.5
         self.events = None   # optional per-layer CUDA events: list of (start, attn_start, attn_end, end)
+        self.last_kv_idx = None
         L, sh = self.layout, self.layout.shard
         D, hid = shape.head_dim, shape.hidden
         gen = torch.Generator(device=self.device)
@@ -221,6 +222,7 @@ class TPDecoder:
         _, summ = ops.qk_norm_rope(k, None, 0.0, cos, sin, norm_mode="none", out=k,
                                    summary="quest" if quest else "mean")
         kv_idx = self._select(q, k, summ)
+        self.last_kv_idx = kv_idx
         ops.block_sparse_attn(q, k, v, kv_idx, self.scale, out=o4)
         return out
 
@@ -237,29 +239,36 @@ class TPDecoder:
 
     # ------------------------------------------------------------------ forward
     @torch.no_grad()
+    def layer(self, h: torch.Tensor, i: int, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+        """Decoder layer i on the residual stream h [S, hidden] (replicated on every rank)."""
+        shape, lw = self.shape, self.layers[i]
+        ev = self.events[i] if self.events is not None else None
+        if ev is not None:
+            ev[0].record()
+        x = rms_norm(h, lw["ln1"], shape.rms_eps)
+        if ev is not None:
+            ev[1].record()
+        a = self._attention(x, lw, cos, sin)
+        if ev is not None:
+            ev[2].record()
+        o = a @ lw["w_o"]
+        self._all_reduce(o)
+        h = h + o
+        x = rms_norm(h, lw["ln2"], shape.rms_eps)
+        m = self._mlp(x, lw)
+        self._all_reduce(m)
+        h = h + m
+        if ev is not None:
+            ev[3].record()
+        return h
+
+    @torch.no_grad()
     def forward(self, ids: torch.Tensor) -> torch.Tensor:
         shape = self.shape
         S = ids.shape[0]
         cos, sin = rotary_tables(S, shape.head_dim, shape.rope_theta, ids.device, self.dtype)
         h = F.embedding(ids, self.embed)
-        for i, lw in enumerate(self.layers):
-            ev = self.events[i] if self.events is not None else None
-            if ev is not None:
-                ev[0].record()
-            x = rms_norm(h, lw["ln1"], shape.rms_eps)
-            if ev is not None:
-                ev[1].record()
-            a = self._attention(x, lw, cos, sin)
-            if ev is not None:
-                ev[2].record()
-            o = a @ lw["w_o"]
-            self._all_reduce(o)
-            h = h + o
-            x = rms_norm(h, lw["ln2"], shape.rms_eps)
-            m = self._mlp(x, lw)
-            self._all_reduce(m)
-            h = h + m
-            if ev is not None:
-                ev[3].record()
+        for i in range(shape.layers):
+            h = self.layer(h, i, cos, sin)
         h = rms_norm(h, self.final_norm, shape.rms_eps)
         return h @ self.lm_head
