@@ -104,7 +104,7 @@ def test_select_bit_exact_vs_oracle(case):
 
 # bf16 cases on the tensor-core scorer, forced onto its single-pass variant (the
 # one long sequences use when the two-pass per-tile arrays do not fit)
-TC_CASES = [c for c in SEL_CASES if c[6] == torch.bfloat16 and c[5] in (64, 128)]
+TC_CASES = [c for c in SEL_CASES if c[6] == torch.bfloat16 and c[5] in (64, 128, 256)]
 
 
 @pytest.mark.parametrize("case", TC_CASES, ids=[c[0] for c in TC_CASES])

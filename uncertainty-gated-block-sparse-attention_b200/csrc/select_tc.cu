@@ -248,6 +248,41 @@ __device__ __forceinline__ float exact_quest_l2(const uint8_t *qp, const uint8_t
     return __fmul_rn(__fadd_rn(ap, an), scale);
 }
 
+// canonical Quest score with the bf16 envelope copies read from L2 one 64-column
+// slab at a time (head dim 256: the whole rows would take 256 registers)
+template <int D>
+__device__ __forceinline__ float exact_quest_l2c(const uint8_t *qp, const uint8_t *qn, const __nv_bfloat16 *kmax,
+                                                 const __nv_bfloat16 *kmin, int R, float scale) {
+    const uint4 *px = reinterpret_cast<const uint4 *>(kmax);
+    const uint4 *py = reinterpret_cast<const uint4 *>(kmin);
+    float ap = 0.f, an = 0.f;
+#pragma unroll 1
+    for (int dh = 0; dh < D / 64; ++dh) {
+        uint4 x[8], y[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            x[i] = __ldg(px + dh * 8 + i);
+            y[i] = __ldg(py + dh * 8 + i);
+        }
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch) {
+            const uint4 a = *reinterpret_cast<const uint4 *>(qp + sw_off(dh, R, ch));
+            const uint4 c = *reinterpret_cast<const uint4 *>(qn + sw_off(dh, R, ch));
+            const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, cw[4] = {c.x, c.y, c.z, c.w};
+            const uint32_t xw[4] = {x[ch].x, x[ch].y, x[ch].z, x[ch].w};
+            const uint32_t yw[4] = {y[ch].x, y[ch].y, y[ch].z, y[ch].w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                ap = fma_bf16_lo(aw[e], xw[e], ap);
+                an = fma_bf16_lo(cw[e], yw[e], an);
+                ap = fma_bf16_hi(aw[e], xw[e], ap);
+                an = fma_bf16_hi(cw[e], yw[e], an);
+            }
+        }
+    }
+    return __fmul_rn(__fadd_rn(ap, an), scale);
+}
+
 // canonical mean score with the fp32 mean read from L2, one 64-element half's
 // loads issued before its chain
 template <int D>
@@ -777,7 +812,7 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
             constexpr int CPC = D / 4, CPI = CPC <= 32 ? 32 / CPC : 1;
             constexpr int kBatch = 16;
             constexpr int kBuf = kBatch * 4 * D;         // bytes per staging buffer
-            static_assert(!TWO_PASS || 8 * 2 * kBuf <= L::STAGES * 2 * L::K_BYTES,
+            static_assert(!TWO_PASS || D > 128 || 8 * 2 * kBuf <= L::STAGES * 2 * L::K_BYTES,
                           "staging exceeds the envelope stages");
             uint8_t *stg = sK + warp * 2 * kBuf;
             const uint32_t lt_mask = (1u << lane) - 1u;
@@ -785,6 +820,8 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
             const __nv_bfloat16 *O1 = p.op1 + ((int64_t)b * p.Hkv + kvh) * p.NB * D;
             auto exact_at = [&](int R, int bk, bool f32) -> float {
                 if (QUEST) {
+                    if (!f32 && D > 128)
+                        return exact_quest_l2c<D>(sQ0, sQ1, O0 + (int64_t)bk * D, O1 + (int64_t)bk * D, R, p.scale);
                     if (!f32)
                         return exact_quest_l2<D>(sQ0, sQ1, O0 + (int64_t)bk * D, O1 + (int64_t)bk * D, R, p.scale);
                     return exact_quest_global<D>(sQ0, sQ1, Bm + (int64_t)bk * D, A + (int64_t)bk * D, R, p.scale);
@@ -884,89 +921,101 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
                 }
             }
             __syncwarp();
-            // batch k0 .. k0 + 15 of the list: lane c < n holds entry c
-            auto entry = [&](int k0, int n) -> uint32_t { return lane < n ? tL[slot(k0 + lane)] : 0u; };
-            // copies the summary rows of a batch into staging buffer buf
-            auto stage = [&](int buf, uint32_t ent, int n) {
-                uint8_t *sb = stg + buf * kBuf;
-#pragma unroll
-                for (int i = 0; i < kBatch / CPI; ++i) {
-                    const int c = i * CPI + lane / CPC, x = lane % CPC;
-                    const int bk = (int)(__shfl_sync(0xffffffffu, ent, c) >> 6);
-                    if (c < n) {
-                        const void *src;
-                        if (QUEST) src = ((x < D / 8) ? O0 : O1) + (int64_t)bk * D + (x % (D / 8)) * 8;
-                        else src = A + (int64_t)bk * D + x * 4;
-                        cp_async16(sb + c * 4 * D + ((x ^ (c & 7)) << 4), src);
+            if constexpr (D <= 128) {
+                // batch k0 .. k0 + 15 of the list: lane c < n holds entry c
+                auto entry = [&](int k0, int n) -> uint32_t { return lane < n ? tL[slot(k0 + lane)] : 0u; };
+                // copies the summary rows of a batch into staging buffer buf
+                auto stage = [&](int buf, uint32_t ent, int n) {
+                    uint8_t *sb = stg + buf * kBuf;
+    #pragma unroll
+                    for (int i = 0; i < kBatch / CPI; ++i) {
+                        const int c = i * CPI + lane / CPC, x = lane % CPC;
+                        const int bk = (int)(__shfl_sync(0xffffffffu, ent, c) >> 6);
+                        if (c < n) {
+                            const void *src;
+                            if (QUEST) src = ((x < D / 8) ? O0 : O1) + (int64_t)bk * D + (x % (D / 8)) * 8;
+                            else src = A + (int64_t)bk * D + x * 4;
+                            cp_async16(sb + c * 4 * D + ((x ^ (c & 7)) << 4), src);
+                        }
                     }
-                }
-                cp_async_commit();
-            };
-            // evaluates a batch from staging buffer buf
-            auto evaluate = [&](int buf, uint32_t ent, int n) {
-                const uint8_t *sb = stg + buf * kBuf;
-                if (QUEST) {
-                    const int c = lane >> 1, half = lane & 1;
-                    const uint32_t e = __shfl_sync(0xffffffffu, ent, c);
-                    float acc = 0.f;
-                    if (c < n) {
-                        const int R = grp * 64 + (int)(e & 63u);
-                        const uint8_t *qs = half ? sQ1 : sQ0;
-                        const uint8_t *ks = sb + c * 4 * D;
-#pragma unroll
-                        for (int i = 0; i < D / 8; ++i) {
-                            const uint4 a = *reinterpret_cast<const uint4 *>(qs + sw_off(i >> 3, R, i & 7));
-                            const uint4 xv =
-                                *reinterpret_cast<const uint4 *>(ks + (((half * (D / 8) + i) ^ (c & 7)) << 4));
-                            const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, xw[4] = {xv.x, xv.y, xv.z, xv.w};
-#pragma unroll
-                            for (int q = 0; q < 4; ++q) {
-                                acc = fma_bf16_lo(aw[q], xw[q], acc);
-                                acc = fma_bf16_hi(aw[q], xw[q], acc);
+                    cp_async_commit();
+                };
+                // evaluates a batch from staging buffer buf
+                auto evaluate = [&](int buf, uint32_t ent, int n) {
+                    const uint8_t *sb = stg + buf * kBuf;
+                    if (QUEST) {
+                        const int c = lane >> 1, half = lane & 1;
+                        const uint32_t e = __shfl_sync(0xffffffffu, ent, c);
+                        float acc = 0.f;
+                        if (c < n) {
+                            const int R = grp * 64 + (int)(e & 63u);
+                            const uint8_t *qs = half ? sQ1 : sQ0;
+                            const uint8_t *ks = sb + c * 4 * D;
+    #pragma unroll
+                            for (int i = 0; i < D / 8; ++i) {
+                                const uint4 a = *reinterpret_cast<const uint4 *>(qs + sw_off(i >> 3, R, i & 7));
+                                const uint4 xv =
+                                    *reinterpret_cast<const uint4 *>(ks + (((half * (D / 8) + i) ^ (c & 7)) << 4));
+                                const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, xw[4] = {xv.x, xv.y, xv.z, xv.w};
+    #pragma unroll
+                                for (int q = 0; q < 4; ++q) {
+                                    acc = fma_bf16_lo(aw[q], xw[q], acc);
+                                    acc = fma_bf16_hi(aw[q], xw[q], acc);
+                                }
                             }
                         }
-                    }
-                    const float an = __shfl_xor_sync(0xffffffffu, acc, 1);
-                    if (c < n && half == 0) out[e >> 6] = __fmul_rn(__fadd_rn(acc, an), p.scale);
-                } else if (lane < n) {
-                    const int c = lane;
-                    const uint32_t e = ent;
-                    const int R = grp * 64 + (int)(e & 63u);
-                    const uint8_t *ks = sb + c * 4 * D;
-                    float acc = 0.f;
-#pragma unroll
-                    for (int i = 0; i < D / 8; ++i) {
-                        const uint4 a = *reinterpret_cast<const uint4 *>(sQ0 + sw_off(i >> 3, R, i & 7));
-                        const float4 x0 = *reinterpret_cast<const float4 *>(ks + (((2 * i) ^ (c & 7)) << 4));
-                        const float4 x1 = *reinterpret_cast<const float4 *>(ks + (((2 * i + 1) ^ (c & 7)) << 4));
-                        const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-                        const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
-#pragma unroll
-                        for (int q = 0; q < 4; ++q) {
-                            acc = __fmaf_rn(bf_lo(aw[q]), xs[2 * q], acc);
-                            acc = __fmaf_rn(bf_hi(aw[q]), xs[2 * q + 1], acc);
+                        const float an = __shfl_xor_sync(0xffffffffu, acc, 1);
+                        if (c < n && half == 0) out[e >> 6] = __fmul_rn(__fadd_rn(acc, an), p.scale);
+                    } else if (lane < n) {
+                        const int c = lane;
+                        const uint32_t e = ent;
+                        const int R = grp * 64 + (int)(e & 63u);
+                        const uint8_t *ks = sb + c * 4 * D;
+                        float acc = 0.f;
+    #pragma unroll
+                        for (int i = 0; i < D / 8; ++i) {
+                            const uint4 a = *reinterpret_cast<const uint4 *>(sQ0 + sw_off(i >> 3, R, i & 7));
+                            const float4 x0 = *reinterpret_cast<const float4 *>(ks + (((2 * i) ^ (c & 7)) << 4));
+                            const float4 x1 = *reinterpret_cast<const float4 *>(ks + (((2 * i + 1) ^ (c & 7)) << 4));
+                            const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                            const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+    #pragma unroll
+                            for (int q = 0; q < 4; ++q) {
+                                acc = __fmaf_rn(bf_lo(aw[q]), xs[2 * q], acc);
+                                acc = __fmaf_rn(bf_hi(aw[q]), xs[2 * q + 1], acc);
+                            }
                         }
+                        out[e >> 6] = __fmul_rn(acc, p.scale);
                     }
-                    out[e >> 6] = __fmul_rn(acc, p.scale);
+                };
+                int cur = 0;
+                int n_cur = min(kBatch, nf);
+                uint32_t e_cur = entry(0, n_cur);
+                stage(0, e_cur, n_cur);
+                for (int k0 = 0; k0 < nf; k0 += kBatch) {
+                    const int n_next = min(kBatch, nf - (k0 + kBatch));
+                    const uint32_t e_next = entry(k0 + kBatch, n_next);
+                    stage(cur ^ 1, e_next, n_next);
+                    cp_async_wait_group1();   // the current batch has landed
+                    __syncwarp();
+                    evaluate(cur, e_cur, n_cur);
+                    __syncwarp();             // this buffer is refilled next
+                    cur ^= 1;
+                    n_cur = n_next;
+                    e_cur = e_next;
                 }
-            };
-            int cur = 0;
-            int n_cur = min(kBatch, nf);
-            uint32_t e_cur = entry(0, n_cur);
-            stage(0, e_cur, n_cur);
-            for (int k0 = 0; k0 < nf; k0 += kBatch) {
-                const int n_next = min(kBatch, nf - (k0 + kBatch));
-                const uint32_t e_next = entry(k0 + kBatch, n_next);
-                stage(cur ^ 1, e_next, n_next);
-                cp_async_wait_group1();   // the current batch has landed
+                cp_async_wait_all();
+            } else {
+                // head dim 256: a lane per candidate, 32 at a time, the candidate's summary
+                // row read from L2 in slabs (its staging would not fit the envelope stages)
+                for (int k0 = 0; k0 < nf; k0 += 32) {
+                    if (k0 + lane < nf) {
+                        const uint32_t e = tL[slot(k0 + lane)];
+                        out[e >> 6] = exact_at(grp * 64 + (int)(e & 63u), (int)(e >> 6), false);
+                    }
+                }
                 __syncwarp();
-                evaluate(cur, e_cur, n_cur);
-                __syncwarp();             // this buffer is refilled next
-                cur ^= 1;
-                n_cur = n_next;
-                e_cur = e_next;
             }
-            cp_async_wait_all();
             for (int k = 0; k < no; ++k) {
                 const uint32_t e = s_other[warp][k], c2 = e & 255u;
                 const uint64_t rows = (c2 & 128u) ? ~0ull : (1ull << (c2 & 63u));
@@ -1208,12 +1257,19 @@ static int launch_score(const CUtensorMap &mQ, const CUtensorMap &mK0, const CUt
     using L = TcLayout<D, QUEST>;
     const size_t base = L::SMEM + 1024;
     if constexpr (D > 128) {
-        // one pass (the candidates' summary rows would not fit the slab stages for pass 2)
-        if (cudaFuncSetAttribute(score_exact_kernel<D, QUEST, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)base) != cudaSuccess)
+        // two passes when the per-tile arrays fit next to the slab stages (pass 2 reads
+        // the candidates' summary rows from L2, a lane per candidate); one pass otherwise
+        const size_t two = base + (size_t)2 * tp.NB * 7 + 16;
+        cudaFuncAttributes fa;
+        if (cudaFuncGetAttributes(&fa, score_exact_kernel<D, QUEST, true>) != cudaSuccess) return UGBSA_ERR_LAUNCH;
+        bool use_two = two + fa.sharedSizeBytes <= 227 * 1024;
+        if (const char *e = getenv("UGBSA_SCORE_ONE_PASS")) use_two = use_two && e[0] != '1';
+        const size_t smem = use_two ? two : base;
+        auto kern = use_two ? score_exact_kernel<D, QUEST, true> : score_exact_kernel<D, QUEST, false>;
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
             return UGBSA_ERR_LAUNCH;
         const int64_t grid = (int64_t)tp.B * tp.Hq * tp.npairs;
-        score_exact_kernel<D, QUEST, false><<<(unsigned)grid, kScoreThreads, base, stream>>>(mQ, mK0, mK1, tp);
+        kern<<<(unsigned)grid, kScoreThreads, smem, stream>>>(mQ, mK0, mK1, tp);
         return cudaGetLastError() == cudaSuccess ? UGBSA_OK : UGBSA_ERR_LAUNCH;
     } else {
         // two passes when the per-tile arrays (2 tiles x NB x (float + byte)) fit next to the pipeline
