@@ -37,21 +37,20 @@ import torch
 
 from . import ops
 
-def pipelined_e2e(host_inputs, compute, out_shape, out_dtype, steps: int, warmup: int = 2):
+def pipelined_e2e(host_inputs, compute, out_shape, out_dtype, steps: int, warmup: int = 2, slots: int = 3):
     """Time `steps` end-to-end steps: each step copies `host_inputs` (pinned) to
     the device, runs compute(device_inputs) -> device output on the current
     stream, and copies the output back to pinned host memory.
 
     Two measurements: serial (copy in, compute, copy out, one step after the
-    other on one stream) and pipelined (three streams, double-buffered device
-    inputs and host outputs: the copy-in of step i+1 and the copy-out of step
-    i-1 run while step i computes, as consecutive requests are served).  The
+    other on one stream) and pipelined (three streams, `slots` device input and
+    host output buffers in rotation: the copy-in of step i+1 and the copy-out of
+    step i-1 run while step i computes, as consecutive requests are served).  The
     pipelined figure is the throughput; every step still moves all its bytes
     inside the timed region.  Returns {"ms": pipelined, "serial_ms": serial}."""
     dev = torch.device("cuda", torch.cuda.current_device())
     cmp = torch.cuda.current_stream()
     h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
-    slots = 2
     d_in = [[torch.empty_like(x, device=dev) for x in host_inputs] for _ in range(slots)]
     h_out = [torch.empty(out_shape, dtype=out_dtype).pin_memory() for _ in range(slots)]
     ev_in = [torch.cuda.Event() for _ in range(slots)]
