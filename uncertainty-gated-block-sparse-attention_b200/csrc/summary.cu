@@ -11,13 +11,14 @@
 //   min/max over the 64 rows, rows >= S count as 0 (the zero padding).
 //
 // Bandwidth-bound: each thread owns 8 consecutive columns of one block and
-// streams the block's 64 rows with 16-byte loads (two for fp32 input), 4 rows
-// in flight held as raw words and converted on use, so a thread stays within 64
-// registers and the whole grid is resident at once (4 CTAs of 256 threads per
-// SM: 592 slots for the 512 CTAs of a 128K x 4-head K; with 78 registers the
-// Quest variant ran in two waves).  Measured at 128K, 4 KV heads, bf16 (CUDA-graph
-// replays): 24.6 us for the mean (86% of HBM), 32.4 us for Quest (67%; its
-// min / max selects cost more issue slots), against 43 us before.  K is read
+// streams the block's 64 rows with 16-byte loads (two for fp32 input), several
+// rows in flight held as raw words, so a thread stays within 64 registers and
+// the whole grid is resident at once (4 CTAs of 256 threads per SM: 592 slots
+// for the 512 CTAs of a 128K x 4-head K).  The Quest envelope of 16-bit K stays
+// in its own format (min / max are exact there): packed two-lane min / max on
+// the raw words, 8 rows in flight, widened to fp32 once.  Measured at 128K, 4
+// KV heads, bf16 (CUDA-graph replays): 24.6 us for the mean (86% of HBM),
+// 27.2 us for Quest (81%; 34 us with the envelope in fp32 registers).  K is read
 // exactly once.
 #include "common.cuh"
 #include "ugbsa_internal.h"
@@ -91,6 +92,98 @@ __device__ __forceinline__ void load8(const __half *p, float (&x)[8]) {
     }
 }
 
+// Packed min / max of two 16-bit lanes (min.bf16x2 / min.f16x2): exact, so the
+// Quest envelope of 16-bit K is kept in its own format (4 words per 8 columns)
+// and widened once at the end.  A NaN in a later row is ignored, as by the
+// ordered compare of the oracle.
+__device__ __forceinline__ uint32_t pmin(uint32_t a, uint32_t b, __nv_bfloat16) {
+    const __nv_bfloat162 r = __hmin2(*reinterpret_cast<const __nv_bfloat162 *>(&a),
+                                     *reinterpret_cast<const __nv_bfloat162 *>(&b));
+    return *reinterpret_cast<const uint32_t *>(&r);
+}
+__device__ __forceinline__ uint32_t pmax(uint32_t a, uint32_t b, __nv_bfloat16) {
+    const __nv_bfloat162 r = __hmax2(*reinterpret_cast<const __nv_bfloat162 *>(&a),
+                                     *reinterpret_cast<const __nv_bfloat162 *>(&b));
+    return *reinterpret_cast<const uint32_t *>(&r);
+}
+__device__ __forceinline__ uint32_t pmin(uint32_t a, uint32_t b, __half) {
+    const __half2 r = __hmin2(*reinterpret_cast<const __half2 *>(&a), *reinterpret_cast<const __half2 *>(&b));
+    return *reinterpret_cast<const uint32_t *>(&r);
+}
+__device__ __forceinline__ uint32_t pmax(uint32_t a, uint32_t b, __half) {
+    const __half2 r = __hmax2(*reinterpret_cast<const __half2 *>(&a), *reinterpret_cast<const __half2 *>(&b));
+    return *reinterpret_cast<const uint32_t *>(&r);
+}
+
+// Quest envelope of 16-bit K: 8 rows in flight (4 registers each), the running
+// min / max in 8 packed registers.
+template <typename T>
+__global__ void __launch_bounds__(256, 4) quest_summary16_kernel(const T *__restrict__ K, int64_t sb, int64_t sh,
+                                                              int64_t ss, int B, int Hkv, int S, int D, int NB,
+                                                              int nb0, int NBo, float *__restrict__ out_a,
+                                                              float *__restrict__ out_b, float *__restrict__ out_norm) {
+    const int tpr = D / 8;
+    const int rows_per_cta = blockDim.x / tpr;
+    const int64_t row_id = (int64_t)blockIdx.x * rows_per_cta + threadIdx.x / tpr;
+    const int part = threadIdx.x % tpr;
+    const int nbl = NB - nb0;
+    const int64_t nrows = (int64_t)B * Hkv * nbl;
+    const bool active = row_id < nrows;
+    const int nb = active ? nb0 + (int)(row_id % nbl) : 0;
+    const int h = active ? (int)((row_id / nbl) % Hkv) : 0;
+    const int b = active ? (int)(row_id / ((int64_t)nbl * Hkv)) : 0;
+    const int64_t out_row = ((int64_t)b * Hkv + h) * NBo + nb;
+    const int d0 = part * 8;
+
+    uint32_t mn[4] = {0u, 0u, 0u, 0u}, mx[4] = {0u, 0u, 0u, 0u};
+    if (active) {
+        const T *base = K + (int64_t)b * sb + (int64_t)h * sh + (int64_t)nb * 64 * ss + d0;
+        const int r_end = min(64, S - nb * 64);   // valid rows of this block (>= 1)
+        const uint4 w0 = __ldg(reinterpret_cast<const uint4 *>(base));
+        mn[0] = mx[0] = w0.x; mn[1] = mx[1] = w0.y; mn[2] = mx[2] = w0.z; mn[3] = mx[3] = w0.w;
+        constexpr int RIF = 8;
+#pragma unroll 1
+        for (int r0 = 0; r0 < 64; r0 += RIF) {
+            uint4 w[RIF];
+#pragma unroll
+            for (int u = 0; u < RIF; ++u) {
+                const int r = r0 + u;
+                w[u] = (r < r_end) ? __ldg(reinterpret_cast<const uint4 *>(base + (int64_t)r * ss))
+                                   : make_uint4(0u, 0u, 0u, 0u);   // zero padding rows
+            }
+#pragma unroll
+            for (int u = 0; u < RIF; ++u) {
+                const uint32_t x[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    mn[i] = pmin(x[i], mn[i], T());
+                    mx[i] = pmax(x[i], mx[i], T());
+                }
+            }
+        }
+    }
+    float fmn[8], fmx[8];
+    Raw8<T> rn, rx;
+    rn.w = make_uint4(mn[0], mn[1], mn[2], mn[3]);
+    rx.w = make_uint4(mx[0], mx[1], mx[2], mx[3]);
+    to_f32(rn, fmn);
+    to_f32(rx, fmx);
+    float sq = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float m = fmaxf(fabsf(fmn[i]), fabsf(fmx[i]));
+        sq = fmaf(m, m, sq);
+    }
+    for (int off = tpr >> 1; off > 0; off >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, off);
+    if (!active) return;
+    const int64_t o = out_row * D + d0;
+    reinterpret_cast<float4 *>(out_a + o)[0] = make_float4(fmn[0], fmn[1], fmn[2], fmn[3]);
+    reinterpret_cast<float4 *>(out_a + o)[1] = make_float4(fmn[4], fmn[5], fmn[6], fmn[7]);
+    reinterpret_cast<float4 *>(out_b + o)[0] = make_float4(fmx[0], fmx[1], fmx[2], fmx[3]);
+    reinterpret_cast<float4 *>(out_b + o)[1] = make_float4(fmx[4], fmx[5], fmx[6], fmx[7]);
+    if (out_norm && part == 0) out_norm[out_row] = sqrtf(sq);
+}
+
 template <typename T, bool QUEST>
 __global__ void __launch_bounds__(256, 4) block_summary_kernel(const T *__restrict__ K, int64_t sb, int64_t sh,
                                                             int64_t ss, int B, int Hkv, int S, int D, int NB,
@@ -116,7 +209,7 @@ __global__ void __launch_bounds__(256, 4) block_summary_kernel(const T *__restri
     if (active) {
         const T *base = K + (int64_t)b * sb + (int64_t)h * sh + d0;
         const int r_end = min(64, S - nb * 64);   // valid rows of this block (>= 1)
-        constexpr int RIF = 4;   // rows in flight
+        constexpr int RIF = (QUEST && sizeof(T) == 4) ? 2 : 4;   // rows in flight (fp32 envelope: 2, within 64 registers)
 #pragma unroll 1
         for (int r0 = 0; r0 < 64; r0 += RIF) {
             Raw8<T> raw[RIF];
@@ -184,9 +277,14 @@ static int launch_summary_t(const T *K, ugbsa_strides ks, int B, int Hkv, int S,
     const int64_t grid = (nrows + rows_per_cta - 1) / rows_per_cta;
     if (grid <= 0) return UGBSA_OK;
     if (grid > 0x7fffffff) return UGBSA_ERR_SHAPE;
-    if (quest)
-        block_summary_kernel<T, true><<<(unsigned)grid, 256, 0, stream>>>(K, ks.b, ks.h, ks.s, B, Hkv, S, D, NB,
-                                                                          nb0, NBo, out_a, out_b, out_norm);
+    if (quest) {
+        if constexpr (sizeof(T) == 2)
+            quest_summary16_kernel<T><<<(unsigned)grid, 256, 0, stream>>>(K, ks.b, ks.h, ks.s, B, Hkv, S, D, NB, nb0,
+                                                                          NBo, out_a, out_b, out_norm);
+        else
+            block_summary_kernel<T, true><<<(unsigned)grid, 256, 0, stream>>>(K, ks.b, ks.h, ks.s, B, Hkv, S, D, NB,
+                                                                              nb0, NBo, out_a, out_b, out_norm);
+    }
     else
         block_summary_kernel<T, false><<<(unsigned)grid, 256, 0, stream>>>(K, ks.b, ks.h, ks.s, B, Hkv, S, D, NB,
                                                                            nb0, NBo, out_a, out_b, out_norm);
