@@ -32,6 +32,12 @@ CASES = [
     ("topk_d256", 2, 4, 1, 8192, 256, torch.bfloat16, dict(mode="topk", budget_blocks=16)),
     ("abs_row_b4", 4, 4, 2, 3000, 128, torch.bfloat16,
      dict(mode="router", router_mode="abs", router_tau=2e-41, budget_blocks=4)),
+    # the bench's geometry at 100K: 1563 blocks over a cluster of 7 CTAs, 7 Q heads per KV head
+    ("quest_gqa7_100k", 1, 28, 4, 100000, 128, torch.bfloat16,
+     dict(mode="router", router_score="quest", budget_blocks=64, k_max=112)),
+    # more than 1024 cells: the prefill finish kernels on one-tile rows
+    ("cells_1280_cell_quantile", 40, 32, 8, 700, 64, torch.bfloat16,
+     dict(mode="router", router_grain="cell", router_quantile=0.3, budget_blocks=2)),
 ]
 
 
@@ -79,6 +85,42 @@ def test_decode_matches_oracle(case):
     assert np.array_equal(trig.cpu().numpy(), want["trigger"])
     out = ops.decode_attn(qd, kd, vd, kv, S, scale)
     _check_attn(out, oracle.decode_attn(q1, k, v, want["kv_idx"], S, scale))
+
+
+@pytest.mark.parametrize("G", [1, 7])
+def test_decode_attn_repeated_and_invalid_ids(G):
+    # hand-made lists: a block repeated within one head's list counts twice (the slot-by-slot
+    # path), ids >= NB and negative ids are skipped
+    B, Hkv, S, D, kmax = 2, 2, 3000, 128, 12
+    Hq = G * Hkv
+    q, k, v, _ = planted_inputs(B, Hq, Hkv, S, D, n_planted=2, seed=21, bf16=True)
+    nb = math.ceil(S / 64)
+    rng = np.random.default_rng(5)
+    kv = rng.integers(0, nb, size=(B, Hq, kmax)).astype(np.int32)
+    kv[0, 0, 3] = kv[0, 0, 1]           # repeat
+    kv[1, -1, 5] = nb                   # sentinel
+    kv[1, -1, 6] = -1                   # negative id
+    kv[0, -1, :] = nb                   # a head with nothing kept
+    q1 = np.ascontiguousarray(q[:, :, -1:])
+    qd, kd, vd = (torch.from_numpy(x).to(DEV).to(torch.bfloat16) for x in (q1, k, v))
+    out = ops.decode_attn(qd, kd, vd, torch.from_numpy(kv).to(DEV), S, D ** -0.5)
+    want = oracle.decode_attn(q1, k, v, kv, S, D ** -0.5)
+    _check_attn(out, want)
+
+
+def test_decode_attn_union_without_repeats():
+    # distinct ids per head, heavily shared across the group (the union path), ragged S
+    B, Hq, Hkv, S, D, kmax = 1, 14, 2, 5000, 64, 20
+    q, k, v, _ = planted_inputs(B, Hq, Hkv, S, D, n_planted=2, seed=22, bf16=True)
+    nb = math.ceil(S / 64)
+    rng = np.random.default_rng(6)
+    kv = np.stack([np.stack([rng.permutation(np.arange(nb // 2))[:kmax] for _ in range(Hq)])
+                   for _ in range(B)]).astype(np.int32)
+    kv[0, :, 0] = nb - 1                 # the ragged last block everywhere
+    q1 = np.ascontiguousarray(q[:, :, -1:])
+    qd, kd, vd = (torch.from_numpy(x).to(DEV).to(torch.bfloat16) for x in (q1, k, v))
+    out = ops.decode_attn(qd, kd, vd, torch.from_numpy(kv).to(DEV), S, D ** -0.5)
+    _check_attn(out, oracle.decode_attn(q1, k, v, kv, S, D ** -0.5))
 
 
 def test_decode_with_every_block_kept_matches_sdpa():

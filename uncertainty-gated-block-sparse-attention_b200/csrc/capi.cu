@@ -320,8 +320,7 @@ static size_t al256s(size_t x) { return (x + 255) / 256 * 256; }
 
 size_t ugbsa_decode_workspace_bytes(int B, int Hq, int S, int D, int kmax) {
     if (B <= 0 || Hq <= 0 || S <= 0 || D <= 0 || kmax <= 0) return 0;
-    const size_t sel = al256s((size_t)B * Hq * 4) + al256s((size_t)B * 4) + al256s(select_finish_workspace_bytes(B, S)) +
-                       al256s((size_t)B * Hq * ((S + 63) / 64) * 4);
+    const size_t sel = al256s((size_t)B * Hq * 4) + al256s((size_t)B * 4) + al256s(select_finish_workspace_bytes(B, S));
     const size_t att = decode_attn_workspace_bytes(B, Hq, D, kmax);
     return sel > att ? sel : att;
 }
@@ -351,11 +350,11 @@ int ugbsa_decode_select(const void *q, int dtype, ugbsa_strides qs, const float 
     float *cells = reinterpret_cast<float *>(ws);
     float *rowsum = reinterpret_cast<float *>(ws + al256s((size_t)B * Hq * 4));
     void *fin_ws = ws + al256s((size_t)B * Hq * 4) + al256s((size_t)B * 4);
-    float *escore = reinterpret_cast<float *>(static_cast<uint8_t *>(fin_ws) +
-                                              al256s(select_finish_workspace_bytes(B, S)));
     if ((rc = launch_decode_select(q, dtype, qs.b, qs.h, summ_a, summ_b, nb_capacity, B, Hq, Hkv, S, D, scale,
-                                   cfg_is_quest(cfg), kb, km, router, kv_idx, cells, escore, st)))
+                                   cfg_is_quest(cfg), kb, km, router, kv_idx, cells, st)))
         return rc;
+    if ((int64_t)B * Hq <= 1024) return launch_decode_finish(cells, B, Hq, S, cfg, kb, km, kv_idx, sigma, trigger, st);
+    // many cells: the prefill finish (row sums, radix quantile, finalize) on one-tile rows
     const bool row = cfg->router_grain == UGBSA_GRAIN_ROW;
     if (router && row && (rc = launch_sigma_rowsum(cells, B, Hq, 1, rowsum, st))) return rc;
     return launch_select_finish_q(cells, (router && row) ? rowsum : cells, B, Hq, Hq, S, 1, 0, 1, 1, cfg, kb, km,

@@ -1289,28 +1289,6 @@ static int launch_score(const CUtensorMap &mQ, const CUtensorMap &mK0, const CUt
     }
 }
 
-// Ranking of exact scores already in escore [B*Hq*Qt, NB] (the decode path: Qt = 1,
-// t_base = NB - 1 makes the cell the sequence's last tile, every block visible).
-int launch_rank_cells(const float *escore, int B, int Hq, int S, int Qt, int t_base, int pair_stride, int k_base,
-                      int kmax, bool router, int32_t *kv_idx, float *sigma_cell, cudaStream_t stream) {
-    const int NB = (S + 63) / 64;
-    RankParams rp;
-    rp.B = B; rp.Hq = Hq; rp.S = S; rp.NB = NB; rp.Qt = Qt;
-    rp.t_base = t_base; rp.pair_stride = pair_stride;
-    int P = 64;
-    while (P < NB) P <<= 1;
-    rp.NBpad = P;
-    rp.k_base = k_base; rp.kmax = kmax; rp.router = router ? 1 : 0;
-    rp.escore = escore; rp.kv_idx = kv_idx; rp.sigma_cell = sigma_cell;
-    const size_t smem = (size_t)P * 12 + 16;
-    if (smem > 227 * 1024) return UGBSA_ERR_SHAPE;
-    if (cudaFuncSetAttribute(rank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-        return UGBSA_ERR_LAUNCH;
-    const int64_t cells = (int64_t)B * Hq * Qt;
-    rank_kernel<<<(unsigned)cells, 256, smem, stream>>>(rp);
-    return cudaGetLastError() == cudaSuccess ? UGBSA_OK : UGBSA_ERR_LAUNCH;
-}
-
 int launch_select_tiles_tc(const void *Q, ugbsa_strides qs, const float *summ_a, const float *summ_b, int B, int Hq,
                            int Hkv, int S, int D, int t_base, int pair_stride, int Sq, float scale, bool quest,
                            int k_base, int kmax, bool router, int32_t *kv_idx, float *sigma_cell, void *scratch,

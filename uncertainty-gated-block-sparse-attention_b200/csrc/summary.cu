@@ -65,6 +65,10 @@ __device__ __forceinline__ void to_f32(const Raw8<float> &r, float (&x)[8]) {
     x[6] = __uint_as_float(r.w[1].z); x[7] = __uint_as_float(r.w[1].w);
 }
 
+__device__ __forceinline__ float to_f(float v) { return v; }
+__device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+
 __device__ __forceinline__ void load8(const float *p, float (&x)[8]) {
     const float4 a = __ldg(reinterpret_cast<const float4 *>(p));
     const float4 b = __ldg(reinterpret_cast<const float4 *>(p) + 1);
@@ -267,6 +271,47 @@ __global__ void __launch_bounds__(256, 4) block_summary_kernel(const T *__restri
     if (out_norm && part == 0) out_norm[out_row] = sqrtf(sq);
 }
 
+// A few blocks (a decode step's growing last block): one CTA per block stages
+// its 64 rows in shared memory with every load in flight at once, then thread d
+// runs column d's sum / min / max down the rows in the canonical order.
+template <typename T, bool QUEST, int D>
+__global__ void __launch_bounds__(256) block_summary_few_kernel(const T *__restrict__ K, int64_t sb, int64_t sh,
+                                                                int64_t ss, int Hkv, int S, int nb0, int nbl, int NBo,
+                                                                float *__restrict__ out_a, float *__restrict__ out_b) {
+    constexpr int CH = D * (int)sizeof(T) / 16;   // 16-byte chunks per row
+    __shared__ __align__(16) T rows[64 * D];
+    const int row_id = blockIdx.x;
+    const int nb = nb0 + row_id % nbl;
+    const int h = (row_id / nbl) % Hkv;
+    const int b = row_id / (nbl * Hkv);
+    const int r_end = min(64, S - nb * 64);
+    const T *base = K + (int64_t)b * sb + (int64_t)h * sh + (int64_t)nb * 64 * ss;
+    for (int i = threadIdx.x; i < 64 * CH; i += 256) {
+        const int r = i / CH, c = i % CH;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);   // rows >= S: the zero padding
+        if (r < r_end) v = __ldg(reinterpret_cast<const uint4 *>(base + (int64_t)r * ss) + c);
+        reinterpret_cast<uint4 *>(rows + r * D)[c] = v;
+    }
+    __syncthreads();
+    const int d = threadIdx.x;
+    if (d >= D) return;
+    const int64_t o = (((int64_t)b * Hkv + h) * NBo + nb) * D + d;
+    if (QUEST) {
+        float mn = to_f(rows[d]), mx = mn;
+        for (int r = 1; r < 64; ++r) {
+            const float x = to_f(rows[r * D + d]);
+            mn = (x < mn) ? x : mn;
+            mx = (x > mx) ? x : mx;
+        }
+        out_a[o] = mn;
+        out_b[o] = mx;
+    } else {
+        float acc = 0.f;
+        for (int r = 0; r < 64; ++r) acc = __fadd_rn(acc, to_f(rows[r * D + d]));
+        out_a[o] = __fmul_rn(acc, 0.015625f);
+    }
+}
+
 template <typename T>
 static int launch_summary_t(const T *K, ugbsa_strides ks, int B, int Hkv, int S, int D, int quest, int nb0, int NBo,
                             float *out_a, float *out_b, float *out_norm, cudaStream_t stream) {
@@ -277,6 +322,25 @@ static int launch_summary_t(const T *K, ugbsa_strides ks, int B, int Hkv, int S,
     const int64_t grid = (nrows + rows_per_cta - 1) / rows_per_cta;
     if (grid <= 0) return UGBSA_OK;
     if (grid > 0x7fffffff) return UGBSA_ERR_SHAPE;
+    // a few blocks and no norms (a decode refresh): one CTA per block, its rows staged at once
+    if (nrows <= 148 && !out_norm && 64 * D * (int)sizeof(T) <= 32768) {
+        const int nbl = NB - nb0;
+#define UGBSA_FEW(DD)                                                                                              \
+        if constexpr (64 * DD * sizeof(T) <= 32768)                                                                \
+        if (D == DD) {                                                                                             \
+            if (quest)                                                                                             \
+                block_summary_few_kernel<T, true, DD><<<(unsigned)nrows, 256, 0, stream>>>(                       \
+                    K, ks.b, ks.h, ks.s, Hkv, S, nb0, nbl, NBo, out_a, out_b);                                     \
+            else                                                                                                   \
+                block_summary_few_kernel<T, false, DD><<<(unsigned)nrows, 256, 0, stream>>>(                      \
+                    K, ks.b, ks.h, ks.s, Hkv, S, nb0, nbl, NBo, out_a, out_b);                                     \
+            return cudaGetLastError() == cudaSuccess ? UGBSA_OK : UGBSA_ERR_LAUNCH;                                \
+        }
+        UGBSA_FEW(64)
+        UGBSA_FEW(128)
+        UGBSA_FEW(256)
+#undef UGBSA_FEW
+    }
     if (quest) {
         if constexpr (sizeof(T) == 2)
             quest_summary16_kernel<T><<<(unsigned)grid, 256, 0, stream>>>(K, ks.b, ks.h, ks.s, B, Hkv, S, D, NB, nb0,

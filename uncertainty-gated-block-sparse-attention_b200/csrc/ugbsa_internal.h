@@ -67,15 +67,16 @@ int launch_select_finish_q(const float *sigma_cell, const float *sigma_all, int 
                            void *workspace, cudaStream_t stream);
 int launch_sigma_rowsum(const float *sigma_cell, int B, int Hq, int Qt, float *rowsum, cudaStream_t stream);
 
-// decode (decode.cu): one query row per head over a cache of S keys
-// escore: [B*Hq, ceil(S/64)] fp32 scratch
+// decode (decode.cu): one query row per head over a cache of S keys.
+// launch_decode_select: scores + top-kmax + sigma per (b, q-head) (a cluster of CTAs per cell);
+// launch_decode_finish: the router over the B x Hq cells (B * Hq <= 1024, else UNSUPPORTED)
 int launch_decode_select(const void *Q, int dtype, int64_t qb, int64_t qh, const float *summ_a, const float *summ_b,
                          int NBs, int B, int Hq, int Hkv, int S, int D, float scale, bool quest, int k_base, int kmax,
-                         bool router, int32_t *kv_idx, float *sigma_cell, float *escore, cudaStream_t stream);
+                         bool router, int32_t *kv_idx, float *sigma_cell, cudaStream_t stream);
+int launch_decode_finish(const float *sigma_cell, int B, int Hq, int S, const ugbsa_selector_config *cfg, int k_base,
+                         int kmax, int32_t *kv_idx, float *sigma_out, uint8_t *trigger_out, cudaStream_t stream);
 int launch_check_bf16_fma(const uint32_t *a, const uint32_t *b, const float *c, float *mixed, float *ref, int n,
                           cudaStream_t stream);
-int launch_rank_cells(const float *escore, int B, int Hq, int S, int Qt, int t_base, int pair_stride, int k_base,
-                      int kmax, bool router, int32_t *kv_idx, float *sigma_cell, cudaStream_t stream);
 int decode_nsplit(int B, int Hq, int kmax);
 size_t decode_attn_workspace_bytes(int B, int Hq, int D, int kmax);
 int launch_decode_attn(const void *Q, const void *K, const void *V, int dtype, ugbsa_strides qs, ugbsa_strides ks,

@@ -965,10 +965,13 @@ def time_decode(q, k, v, cfg: ops.SelectorConfig, scale: float, reps: int = 20):
     """One decode step per layer at this cache length (the last query row of
     each head against the whole K/V): the block-sparse decode (summary refresh
     of the last block, selection, attention) against torch SDPA over the whole
-    cache (the reference's decode), CUDA events, ms per step."""
+    cache (the reference's decode), CUDA events, ms per step.  Each stage is
+    also captured alone in a CUDA graph and replayed, which gives its GPU time
+    without the host's per-call cost."""
     import torch.nn.functional as F
     B, Hq, _, D = q.shape
     Hkv, S = k.shape[1], k.shape[2]
+    G = Hq // Hkv
     q1 = q[:, :, -1:].contiguous()
     summ = ops.block_summary(k, cfg.quest)
     nb = math.ceil(S / 64)
@@ -985,38 +988,51 @@ def time_decode(q, k, v, cfg: ops.SelectorConfig, scale: float, reps: int = 20):
         torch.cuda.synchronize()
         return s.elapsed_time(e) / reps, r
 
-    def sparse():
+    def graphed(fn):
+        try:
+            g = torch.cuda.CUDAGraph()
+            side = torch.cuda.Stream()
+            side.wait_stream(st)
+            with torch.cuda.stream(side):
+                fn()                      # warm the allocator pool on the capture stream
+                with torch.cuda.graph(g, stream=side):
+                    fn()
+            st.wait_stream(side)
+            return timed(lambda: g.replay())[0]
+        except Exception:                 # capture unsupported here: eager only
+            return None
+
+    def refresh():
         ops.block_summary_update(k, cfg.quest, summ, nb - 1)
+
+    def sparse():
+        refresh()
         kv = ops.decode_select(q1, summ, S, Hkv, scale, cfg)
         return ops.decode_attn(q1, k, v, kv, S, scale), kv
 
     t_sparse, (_, kv) = timed(sparse)
     t_sel, _ = timed(lambda: ops.decode_select(q1, summ, S, Hkv, scale, cfg))
     t_att, _ = timed(lambda: ops.decode_attn(q1, k, v, kv, S, scale))
-    # the same step captured in a CUDA graph: the GPU time without the host's
-    # per-call launch cost (five small kernels and two host calls per step)
-    t_graph = None
-    try:
-        g = torch.cuda.CUDAGraph()
-        side = torch.cuda.Stream()
-        side.wait_stream(st)
-        with torch.cuda.stream(side):
-            sparse()                      # warm the allocator pool on the capture stream
-            with torch.cuda.graph(g, stream=side):
-                sparse()
-        st.wait_stream(side)
-        t_graph, _ = timed(lambda: g.replay())
-    except Exception:                     # capture unsupported here: report eager only
-        t_graph = None
+    t_graph = graphed(sparse)
+    g_refresh = graphed(refresh)
+    g_sel = graphed(lambda: ops.decode_select(q1, summ, S, Hkv, scale, cfg))
+    g_att = graphed(lambda: ops.decode_attn(q1, k, v, kv, S, scale))
     t_dense, _ = timed(lambda: F.scaled_dot_product_attention(q1, k, v, scale=scale, enable_gqa=Hq != Hkv))
-    kept = ((kv >= 0) & (kv < nb)).sum().item()
+    valid = (kv >= 0) & (kv < nb)
+    kept = valid.sum().item()
+    # the attention reads each KV group's union of its heads' lists once
+    ids = torch.where(valid, kv, torch.full_like(kv, nb)).view(B, Hkv, G * kv.shape[-1])
+    union = sum(int(torch.unique(ids[b_, h_]).numel()) - int((ids[b_, h_] == nb).any())
+                for b_ in range(B) for h_ in range(Hkv))
     el = k.element_size()
-    kv_bytes_per_qhead = kept * 64 * D * 2 * el                       # K and V of the kept blocks, every Q head
+    union_bytes = union * 64 * D * 2 * el
     summ_bytes = B * Hkv * nb * D * 4 * (2 if cfg.quest else 1)
     return {"sparse_ms": t_sparse, "sparse_graph_ms": t_graph, "select_ms": t_sel, "attn_ms": t_att,
+            "graph_stage_ms": {"refresh": g_refresh, "select": g_sel, "attn": g_att},
             "dense_sdpa_ms": t_dense,
-            "kept_blocks_per_head": kept / (B * Hq), "attn_kv_bytes": kv_bytes_per_qhead,
-            "attn_GB_s": kv_bytes_per_qhead / (t_att / 1e3) / 1e9, "summary_bytes": summ_bytes}
+            "kept_blocks_per_head": kept / (B * Hq), "union_blocks_per_group": union / (B * Hkv),
+            "attn_kv_bytes": union_bytes,
+            "attn_GB_s": (union_bytes / (g_att / 1e3) / 1e9) if g_att else None, "summary_bytes": summ_bytes}
 
 
 def time_dense(q, k, v, scale, reps: int = 3):
