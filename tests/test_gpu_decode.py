@@ -38,6 +38,12 @@ CASES = [
     # more than 1024 cells: the prefill finish kernels on one-tile rows
     ("cells_1280_cell_quantile", 40, 32, 8, 700, 64, torch.bfloat16,
      dict(mode="router", router_grain="cell", router_quantile=0.3, budget_blocks=2)),
+    # 12 Q heads per KV head: the 16-accumulator selection, two heads ranked per cluster CTA
+    ("gqa12_d64_quest", 1, 12, 1, 3000, 64, torch.bfloat16,
+     dict(mode="router", router_score="quest", budget_blocks=8)),
+    # head dim 256 in fp16: one staged round in flight
+    ("gqa4_d256_quest_fp16", 1, 8, 2, 20000, 256, torch.float16,
+     dict(mode="router", router_score="quest", budget_blocks=16)),
 ]
 
 
@@ -105,6 +111,23 @@ def test_decode_attn_repeated_and_invalid_ids(G):
     qd, kd, vd = (torch.from_numpy(x).to(DEV).to(torch.bfloat16) for x in (q1, k, v))
     out = ops.decode_attn(qd, kd, vd, torch.from_numpy(kv).to(DEV), S, D ** -0.5)
     want = oracle.decode_attn(q1, k, v, kv, S, D ** -0.5)
+    _check_attn(out, want)
+
+
+def test_decode_attn_past_bitmap_limit():
+    # more than 8192 blocks: the union bitmaps do not fit and the kernel goes slot by slot
+    B, Hq, Hkv, D, kmax = 1, 2, 1, 64, 16
+    S = 8192 * 64 + 100
+    nb = math.ceil(S / 64)
+    g = torch.Generator().manual_seed(23)
+    k = torch.randn((B, Hkv, S, D), generator=g).to(torch.bfloat16)
+    v = torch.randn((B, Hkv, S, D), generator=g).to(torch.bfloat16)
+    q = torch.randn((B, Hq, 1, D), generator=g).to(torch.bfloat16)
+    rng = np.random.default_rng(7)
+    kv = np.stack([np.stack([rng.permutation(nb)[:kmax] for _ in range(Hq)])]).astype(np.int32)
+    kv[0, 0, 0] = nb - 1                 # the ragged last block
+    out = ops.decode_attn(q.to(DEV), k.to(DEV), v.to(DEV), torch.from_numpy(kv).to(DEV), S, D ** -0.5)
+    want = oracle.decode_attn(q.float().numpy(), k.float().numpy(), v.float().numpy(), kv, S, D ** -0.5)
     _check_attn(out, want)
 
 

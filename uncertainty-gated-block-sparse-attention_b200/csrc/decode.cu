@@ -74,20 +74,6 @@ __device__ __forceinline__ uint32_t asc_key_dec(float v) {
     return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
 
-// an empty volatile statement that redefines v: placed after a batch of volatile
-// loads, it keeps every use of the batch behind the last load's issue
-__device__ __forceinline__ void hold_v4(float4 &v) {
-    asm volatile("" : "+f"(v.x), "+f"(v.y), "+f"(v.z), "+f"(v.w));
-}
-
-__device__ __forceinline__ float4 ld_nc_v4(const float4 *p) {
-    float4 v;
-    asm volatile("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];"
-                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                 : "l"(p));
-    return v;
-}
-
 }  // namespace
 
 // ------------------------------------------------------------------ selection
