@@ -79,7 +79,7 @@ __device__ __forceinline__ uint32_t asc_key_dec(float v) {
 // ------------------------------------------------------------------ selection
 constexpr int kDecMaxGroup = 16;
 constexpr int kDecSelThreads = 512;
-constexpr int kDecMaxCluster = 8;
+constexpr int kDecMaxCluster = 16;   // 16 needs the non-portable cluster size; 8 otherwise
 
 struct DecSelParams {
     int B, Hq, Hkv, G, S, NB, NBs, CL, chunk, hpc;   // hpc: heads ranked per CTA (head g by CTA g % CL)
@@ -256,59 +256,114 @@ __global__ void __launch_bounds__(kDecSelThreads, 1) decode_select_kernel(const 
             s_val[0] = s_val[1] = s_val[2] = -INFINITY;
         }
         __syncthreads();
-        // V = the kmax-th largest key (descending radix selection, a histogram per warp)
+        // V: a key at or below the kmax-th largest (every candidate of the top kmax has
+        // a key >= V; a few extra candidates only cost the counting rank below).
+        // The forced sink / own blocks take their slots first: V is the (kmax - 2)-th
+        // largest of the other keys, by a descending radix selection that starts at the
+        // first bit where their smallest and largest key differ and stops once the bin
+        // holding V has at most 16 keys (its lower edge is then V).  Keys at or above
+        // the forced value (FLT_MAX, infinite or NaN scores) can push a forced block out
+        // of the top kmax; then the selection runs over all keys instead.
         uint32_t V = 0u;
         if (NB > p.kmax) {
-            for (int shift = 24; shift >= 0; shift -= 8) {
-                for (int i = lane; i < 256; i += 32) whist[warp][i] = 0u;
-                __syncwarp();
-                const uint32_t prefix = s_prefix, mask = s_mask;
-                for (int j = tid; j < NB; j += kDecSelThreads) {
-                    const uint32_t u = hk[j];
-                    if ((u & mask) == prefix) atomicAdd(&whist[warp][255u - ((u >> shift) & 255u)], 1u);
-                }
-                __syncthreads();
-                if (tid < 256) {
-                    uint32_t c = 0u;
+            const uint32_t kforced = ordered_key(FLT_MAX);
+            uint32_t kmn = 0xffffffffu, kmx = 0u;
+            for (int j = tid; j < NB; j += kDecSelThreads) {
+                if (j == 0 || j == NB - 1) continue;
+                const uint32_t u = hk[j];
+                kmn = min(kmn, u);
+                kmx = max(kmx, u);
+            }
+            kmn = __reduce_min_sync(0xffffffffu, kmn);
+            kmx = __reduce_max_sync(0xffffffffu, kmx);
+            if (lane == 0) {
+                whist[warp][0] = kmn;
+                whist[warp][1] = kmx;
+            }
+            __syncthreads();
+            kmn = 0xffffffffu;
+            kmx = 0u;
 #pragma unroll
-                    for (int w = 0; w < NW; ++w) c += whist[w][tid];
-                    tot[tid] = c;
-                }
-                __syncthreads();
-                if (warp == 0) {
-                    uint32_t cnt[8], sum = 0u;
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        cnt[e] = tot[8 * lane + e];
-                        sum += cnt[e];
+            for (int w = 0; w < NW; ++w) {
+                kmn = min(kmn, whist[w][0]);
+                kmx = max(kmx, whist[w][1]);
+            }
+            __syncthreads();
+            const bool excl_forced = kmx < kforced;   // no other key ties with or passes the forced ones
+            const int nforced = NB >= 2 ? 2 : 1;
+            int k = excl_forced ? p.kmax - nforced : p.kmax;
+            if (!excl_forced) {
+                kmn = 0u;
+                kmx = 0xffffffffu;
+            }
+            if (k <= 0) {
+                V = kforced;
+            } else if (kmn == kmx) {
+                V = kmn;
+            } else {
+                int lowbit = 32 - __clz(kmn ^ kmx);   // bits below are not yet fixed
+                uint32_t prefix = (uint32_t)((unsigned long long)kmx & (~0ull << lowbit));
+                for (;;) {
+                    const int shift = max(lowbit - 8, 0);
+                    const uint32_t nbins = 1u << (lowbit - shift);
+                    const uint32_t himask = (uint32_t)(~0ull << lowbit);
+                    for (int i = lane; i < 256; i += 32) whist[warp][i] = 0u;
+                    __syncwarp();
+                    for (int j = tid; j < NB; j += kDecSelThreads) {
+                        if (excl_forced && (j == 0 || j == NB - 1)) continue;
+                        const uint32_t u = hk[j];
+                        if ((u & himask) == prefix)
+                            atomicAdd(&whist[warp][(nbins - 1u) - ((u >> shift) & (nbins - 1u))], 1u);
                     }
-                    uint32_t incl = sum;
+                    __syncthreads();
+                    if (tid < 256) {
+                        uint32_t c = 0u;
 #pragma unroll
-                    for (int off = 1; off < 32; off <<= 1) {
-                        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, off);
-                        if (lane >= off) incl += y;
+                        for (int w = 0; w < NW; ++w) c += whist[w][tid];
+                        tot[tid] = c;
                     }
-                    const uint32_t excl = incl - sum;
-                    const uint32_t k = (uint32_t)s_k;
-                    if (excl < k && k <= incl) {
-                        uint32_t run = excl;
-                        int bin = 8 * lane + 7;
+                    __syncthreads();
+                    if (warp == 0) {
+                        uint32_t cnt[8], sum = 0u;
 #pragma unroll
                         for (int e = 0; e < 8; ++e) {
-                            if (run + cnt[e] >= k) {
-                                bin = 8 * lane + e;
-                                break;
-                            }
-                            run += cnt[e];
+                            cnt[e] = tot[8 * lane + e];
+                            sum += cnt[e];
                         }
-                        s_k = (int)(k - run);
-                        s_prefix = prefix | ((255u - (uint32_t)bin) << shift);
-                        s_mask = mask | (255u << shift);
+                        uint32_t incl = sum;
+#pragma unroll
+                        for (int off = 1; off < 32; off <<= 1) {
+                            const uint32_t y = __shfl_up_sync(0xffffffffu, incl, off);
+                            if (lane >= off) incl += y;
+                        }
+                        const uint32_t excl = incl - sum;
+                        if (excl < (uint32_t)k && (uint32_t)k <= incl) {
+                            uint32_t run = excl, selc = 0u;
+                            int bin = 8 * lane + 7;
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) {
+                                if (run + cnt[e] >= (uint32_t)k) {
+                                    bin = 8 * lane + e;
+                                    selc = cnt[e];
+                                    break;
+                                }
+                                run += cnt[e];
+                            }
+                            s_k = (int)((uint32_t)k - run);
+                            s_prefix = prefix | (((nbins - 1u) - (uint32_t)bin) << shift);
+                            s_mask = selc;
+                        }
                     }
+                    __syncthreads();
+                    prefix = s_prefix;
+                    k = s_k;
+                    lowbit = shift;
+                    const uint32_t selc = s_mask;
+                    __syncthreads();   // s_prefix / s_k / s_mask are rewritten by the next pass
+                    if (selc <= 16u || shift == 0) break;
                 }
-                __syncthreads();
+                V = prefix;
             }
-            V = s_prefix;
         }
         // candidates: key >= V (every block when NB <= kmax)
         for (int jb = tid - lane; jb < NB; jb += kDecSelThreads) {
@@ -440,49 +495,22 @@ int launch_decode_select(const void *Q, int dtype, int64_t qb, int64_t qh, const
     if (D != 64 && D != 128 && D != 256) return UGBSA_ERR_UNSUPPORTED;
     DecSelParams p;
     p.B = B; p.Hq = Hq; p.Hkv = Hkv; p.G = Hq / Hkv; p.S = S; p.NB = (S + 63) / 64; p.NBs = NBs;
-    // a cluster per (b, kv head): up to 8 CTAs, enough for the group's heads or 256 rows each
-    int cl = (p.NB + 255) / 256;
+    // a cluster per (b, kv head): enough CTAs for the group's heads or 128 summary rows
+    // each, up to 16 when the device schedules clusters of 16 (else 8)
+    int cl = (p.NB + 127) / 128;
     if (cl < p.G) cl = p.G;
-    p.CL = cl > kDecMaxCluster ? kDecMaxCluster : cl;
-    p.chunk = (p.NB + p.CL - 1) / p.CL;
-    p.hpc = (p.G + p.CL - 1) / p.CL;
+    if (cl > 8) cl = kDecMaxCluster;
     p.qb = qb; p.qh = qh; p.scale = scale;
     p.k_base = k_base; p.kmax = kmax; p.router = router ? 1 : 0;
     p.summ_a = summ_a; p.summ_b = summ_b; p.kv_idx = kv_idx; p.sigma_cell = sigma_cell;
     const int nch = quest ? 2 : 1;
-    // as many staged rounds (two 32-row tiles of both operands) in flight as the shared
-    // memory allows (up to two)
-    const size_t tile = (size_t)2 * 2 * 32 * D * 4;
-    const size_t rest = (size_t)nch * p.G * D * 4 + (size_t)p.hpc * ((p.NB + 3) & ~3) * 4 + (size_t)32 * 64 * 4;
-    const size_t budget_bytes = 200 * 1024;
-    int nbuf = kDecSelMaxBufs;
-    while (nbuf > 1 && (size_t)nbuf * tile + rest > budget_bytes) --nbuf;
-    p.nbuf = nbuf;
-    const size_t tiles = (size_t)nbuf * tile > (size_t)p.NB * 8 ? (size_t)nbuf * tile : (size_t)p.NB * 8;
-    const size_t smem = tiles + rest;
-    if (smem > budget_bytes) return UGBSA_ERR_SHAPE;
-    cudaLaunchConfig_t lc = {};
-    lc.gridDim = dim3((unsigned)(B * Hkv * p.CL));
-    lc.blockDim = dim3(kDecSelThreads);
-    lc.dynamicSmemBytes = smem;
-    lc.stream = stream;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = (unsigned)p.CL;
-    at[0].val.clusterDim.y = 1;
-    at[0].val.clusterDim.z = 1;
-    lc.attrs = at;
-    lc.numAttrs = 1;
-    cudaError_t e = cudaErrorInvalidValue;
-    // the kernel keeps GM accumulators per lane: the group size rounded up to 4, 8 or 16
+    // the kernel for this shape (GM accumulators per lane: the group size rounded up to 4, 8 or 16)
     const int gm = p.G <= 4 ? 4 : (p.G <= 8 ? 8 : 16);
+    void (*kern)(const void *, DecSelParams) = nullptr;
 #define UGBSA_DEC_SEL_G(TT, DD, GG)                                                                                \
-    if (gm == GG) {                                                                                                \
-        auto k = quest ? decode_select_kernel<TT, true, DD, GG> : decode_select_kernel<TT, false, DD, GG>;         \
-        if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)        \
-            return UGBSA_ERR_LAUNCH;                                                                               \
-        e = cudaLaunchKernelEx(&lc, k, (const TT *)Q, p);                                                          \
-    }
+    if (gm == GG)                                                                                                  \
+        kern = reinterpret_cast<void (*)(const void *, DecSelParams)>(                                             \
+            quest ? decode_select_kernel<TT, true, DD, GG> : decode_select_kernel<TT, false, DD, GG>);
 #define UGBSA_DEC_SEL(TT, DD)                                                                                      \
     if (D == DD) {                                                                                                 \
         UGBSA_DEC_SEL_G(TT, DD, 4) else UGBSA_DEC_SEL_G(TT, DD, 8) else UGBSA_DEC_SEL_G(TT, DD, 16)                \
@@ -497,6 +525,47 @@ int launch_decode_select(const void *Q, int dtype, int64_t qb, int64_t qh, const
 #undef UGBSA_DEC_SEL_T
 #undef UGBSA_DEC_SEL
 #undef UGBSA_DEC_SEL_G
+    if (!kern) return UGBSA_ERR_UNSUPPORTED;
+    if (cl > 8 && cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+        cl = 8;
+    // as many staged rounds (two 32-row tiles of both operands) in flight as the shared
+    // memory allows (up to two); the cluster shrinks to 8 if the device cannot place 16
+    const size_t tile = (size_t)2 * 2 * 32 * D * 4;
+    const size_t budget_bytes = 200 * 1024;
+    cudaLaunchConfig_t lc = {};
+    cudaLaunchAttribute at[1];
+    size_t smem = 0;
+    for (int attempt = 0; attempt < 2; ++attempt) {
+        p.CL = cl;
+        p.chunk = (p.NB + p.CL - 1) / p.CL;
+        p.hpc = (p.G + p.CL - 1) / p.CL;
+        const size_t rest = (size_t)nch * p.G * D * 4 + (size_t)p.hpc * ((p.NB + 3) & ~3) * 4 + (size_t)32 * 64 * 4;
+        int nbuf = kDecSelMaxBufs;
+        while (nbuf > 1 && (size_t)nbuf * tile + rest > budget_bytes) --nbuf;
+        p.nbuf = nbuf;
+        const size_t tiles = (size_t)nbuf * tile > (size_t)p.NB * 8 ? (size_t)nbuf * tile : (size_t)p.NB * 8;
+        smem = tiles + rest;
+        if (smem > budget_bytes) return UGBSA_ERR_SHAPE;
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+            return UGBSA_ERR_LAUNCH;
+        lc = cudaLaunchConfig_t{};
+        lc.gridDim = dim3((unsigned)(B * Hkv * p.CL));
+        lc.blockDim = dim3(kDecSelThreads);
+        lc.dynamicSmemBytes = smem;
+        lc.stream = stream;
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = (unsigned)p.CL;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        lc.attrs = at;
+        lc.numAttrs = 1;
+        if (cl <= 8) break;
+        int nclusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&nclusters, kern, &lc) == cudaSuccess && nclusters > 0) break;
+        cudaGetLastError();
+        cl = 8;
+    }
+    const cudaError_t e = cudaLaunchKernelEx(&lc, kern, Q, p);
     return e == cudaSuccess ? UGBSA_OK : UGBSA_ERR_LAUNCH;
 }
 
