@@ -200,6 +200,15 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Programmatic dependent launch: a kernel launched with the programmatic
+// stream-serialization attribute may become resident while its predecessor in the
+// stream still runs; grid_dep_wait() returns once that predecessor has completed and
+// its memory is visible (at once when there is no such dependency).
+// grid_dep_launch() lets this grid's dependent start launching (it takes effect when
+// every CTA of the grid has issued it or exited).
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

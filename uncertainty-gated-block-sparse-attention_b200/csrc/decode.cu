@@ -47,6 +47,7 @@
 #include <cfloat>
 #include <cstdlib>
 #include <type_traits>
+#include <utility>
 
 #include "common.cuh"
 #include "ugbsa_internal.h"
@@ -75,6 +76,25 @@ __device__ __forceinline__ uint32_t asc_key_dec(float v) {
 }
 
 }  // namespace
+
+// host: launch with the programmatic stream-serialization attribute (the kernel may
+// become resident while its predecessor in the stream finishes; it calls
+// grid_dep_wait() before reading that predecessor's output)
+template <typename... KArgs, typename... Args>
+static int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                      Args &&...args) {
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = grid;
+    lc.blockDim = block;
+    lc.dynamicSmemBytes = smem;
+    lc.stream = stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = at;
+    lc.numAttrs = 1;
+    return cudaLaunchKernelEx(&lc, kern, std::forward<Args>(args)...) == cudaSuccess ? UGBSA_OK : UGBSA_ERR_LAUNCH;
+}
 
 // ------------------------------------------------------------------ selection
 constexpr int kDecMaxGroup = 16;
@@ -142,6 +162,8 @@ __global__ void __launch_bounds__(kDecSelThreads, 1) decode_select_kernel(const 
     __shared__ uint32_t s_prefix, s_mask;
     __shared__ int s_k, s_n;
     __shared__ float s_val[3];
+    grid_dep_launch();
+    grid_dep_wait();   // the summaries (a refresh just before) are complete
 
     // the group's query rows: Quest max(q,0) and min(q,0); mean q
     for (int i = tid; i < G * D; i += kDecSelThreads) {
@@ -435,6 +457,8 @@ __global__ void __launch_bounds__(1024) decode_finish_kernel(const DecFinParams 
     __shared__ float s_th;
     const int tid = threadIdx.x;
     const int ncell = p.B * p.Hq;
+    grid_dep_launch();
+    grid_dep_wait();   // the selection's margins and lists are complete
     if (tid < ncell) s_cell[tid] = p.sigma_cell[tid];   // one load per thread, all in flight
     __syncthreads();
     if (p.router) {
@@ -533,7 +557,7 @@ int launch_decode_select(const void *Q, int dtype, int64_t qb, int64_t qh, const
     const size_t tile = (size_t)2 * 2 * 32 * D * 4;
     const size_t budget_bytes = 200 * 1024;
     cudaLaunchConfig_t lc = {};
-    cudaLaunchAttribute at[1];
+    cudaLaunchAttribute at[2];
     size_t smem = 0;
     for (int attempt = 0; attempt < 2; ++attempt) {
         p.CL = cl;
@@ -557,8 +581,10 @@ int launch_decode_select(const void *Q, int dtype, int64_t qb, int64_t qh, const
         at[0].val.clusterDim.x = (unsigned)p.CL;
         at[0].val.clusterDim.y = 1;
         at[0].val.clusterDim.z = 1;
+        at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // may overlap the refresh's tail
+        at[1].val.programmaticStreamSerializationAllowed = 1;
         lc.attrs = at;
-        lc.numAttrs = 1;
+        lc.numAttrs = 2;
         if (cl <= 8) break;
         int nclusters = 0;
         if (cudaOccupancyMaxActiveClusters(&nclusters, kern, &lc) == cudaSuccess && nclusters > 0) break;
@@ -586,8 +612,7 @@ int launch_decode_finish(const float *sigma_cell, int B, int Hq, int S, const ug
     p.kq = kq;
     p.tau = (float)cfg->router_tau;
     p.sigma_cell = sigma_cell; p.kv_idx = kv_idx; p.sigma_out = sigma_out; p.trigger_out = trigger_out;
-    decode_finish_kernel<<<1, 1024, 0, stream>>>(p);
-    return cudaGetLastError() == cudaSuccess ? UGBSA_OK : UGBSA_ERR_LAUNCH;
+    return launch_pdl(decode_finish_kernel, dim3(1), dim3(1024), 0, stream, p);
 }
 
 // ------------------------------------------------------------------ attention
@@ -680,6 +705,8 @@ __global__ void __launch_bounds__(kDecAttnThreads) decode_group_attn_kernel(cons
     __shared__ __align__(8) uint64_t bar_full[STAGES];
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    grid_dep_launch();
+    grid_dep_wait();   // kv_idx (the selection's finish just before) is complete
     const int grp = blockIdx.x / p.nsplit, split = blockIdx.x % p.nsplit;
     const int kvh = grp % p.Hkv, b = grp / p.Hkv;
     const int G = p.G;
@@ -983,6 +1010,7 @@ __global__ void __launch_bounds__(D) decode_combine_kernel(const DecAttnParams p
     const int cell = blockIdx.x;
     const int h = cell % p.Hq, b = cell / p.Hq;
     const int d = threadIdx.x;
+    grid_dep_wait();   // every split's partials are written
     const int nfl = p.nsplit * (D + 2);
     const float *base = p.part + (int64_t)cell * nfl;
     float *s_f = s_part + ((nfl + 3) & ~3);
@@ -1103,13 +1131,12 @@ int launch_decode_attn(const void *Q, const void *K, const void *V, int dtype, u
         auto k = decode_group_attn_kernel<TT, DD>;                                                                 \
         if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)        \
             return UGBSA_ERR_LAUNCH;                                                                               \
-        k<<<grid, kDecAttnThreads, smem, stream>>>((const TT *)Q, mapK, mapV, p);                                  \
-        if (cudaGetLastError() != cudaSuccess) return UGBSA_ERR_LAUNCH;                                            \
+        int rc_ = launch_pdl(k, grid, dim3(kDecAttnThreads), smem, stream, (const TT *)Q, mapK, mapV, p);          \
+        if (rc_ != UGBSA_OK) return rc_;                                                                           \
         auto kc = decode_combine_kernel<TT, DD>;                                                                   \
         if (cudaFuncSetAttribute(kc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem) != cudaSuccess)      \
             return UGBSA_ERR_LAUNCH;                                                                               \
-        kc<<<(unsigned)(B * Hq), DD, csmem, stream>>>(p, (TT *)out);                                               \
-        return cudaGetLastError() == cudaSuccess ? UGBSA_OK : UGBSA_ERR_LAUNCH;                                    \
+        return launch_pdl(kc, dim3((unsigned)(B * Hq)), dim3(DD), csmem, stream, p, (TT *)out);                    \
     }
     if (dtype == UGBSA_BF16) {
         UGBSA_DEC_ATTN(__nv_bfloat16, 64)

@@ -280,6 +280,7 @@ __global__ void __launch_bounds__(256) block_summary_few_kernel(const T *__restr
                                                                 float *__restrict__ out_a, float *__restrict__ out_b) {
     constexpr int CH = D * (int)sizeof(T) / 16;   // 16-byte chunks per row
     __shared__ __align__(16) T rows[64 * D];
+    grid_dep_launch();   // a decode step's selection may become resident meanwhile
     const int row_id = blockIdx.x;
     const int nb = nb0 + row_id % nbl;
     const int h = (row_id / nbl) % Hkv;
