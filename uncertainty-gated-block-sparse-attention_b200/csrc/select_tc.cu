@@ -1091,8 +1091,10 @@ __device__ void bitonic_desc_256(uint64_t *keys, int P) {
 __global__ void __launch_bounds__(256) rank_kernel(const RankParams p) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
     uint64_t *keys = reinterpret_cast<uint64_t *>(smem_raw);
-    uint32_t *key32 = reinterpret_cast<uint32_t *>(keys + p.NBpad);
+    uint32_t *key32 = reinterpret_cast<uint32_t *>(keys + (p.NBpad > 1024 ? p.NBpad : 1024));
     __shared__ uint32_t hist[256];
+    // per-warp histograms of the radix passes, over the sort keys (written only after the passes)
+    uint32_t(*whist)[256] = reinterpret_cast<uint32_t(*)[256]>(keys);
     __shared__ uint32_t s_prefix, s_mask;
     __shared__ int s_k, s_n;
 
@@ -1107,7 +1109,21 @@ __global__ void __launch_bounds__(256) rank_kernel(const RankParams p) {
     const int64_t cell = ((int64_t)b * p.Hq + h) * p.Qt + t;
     const float *es = p.escore + cell * p.NB;
 
-    for (int j = tid; j < nvis; j += 256) key32[j] = (j == 0 || j == self_blk) ? ord_key(FLT_MAX) : ord_key(es[j]);
+    // the visible blocks' keys: eight loads per thread issued together (the score
+    // array is read once, from memory)
+    for (int j0 = 0; j0 < nvis; j0 += 8 * 256) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int j = j0 + u * 256 + tid;
+            v[u] = (j < nvis) ? __ldcs(es + j) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int j = j0 + u * 256 + tid;
+            if (j < nvis) key32[j] = (j == 0 || j == self_blk) ? ord_key(FLT_MAX) : ord_key(v[u]);
+        }
+    }
     if (tid == 0) {
         s_prefix = 0;
         s_mask = 0;
@@ -1118,22 +1134,22 @@ __global__ void __launch_bounds__(256) rank_kernel(const RankParams p) {
     // V = kmax-th largest value key (descending radix select); all visible when nvis <= kmax
     uint32_t V = 0u;
     if (nvis > p.kmax) {
+        const int lane = tid & 31, warp = tid >> 5;
         for (int shift = 24; shift >= 0; shift -= 8) {
-            hist[tid] = 0;
-            __syncthreads();
+            // a histogram per warp: no cross-warp atomics (the keys cluster in few bins)
+            for (int i = lane; i < 256; i += 32) whist[warp][i] = 0u;
+            __syncwarp();
             const uint32_t prefix = s_prefix, mask = s_mask;
-            // warp-aggregated: lanes with the same bin add once (scores cluster in few top bins)
-            const int lane = tid & 31;
-            for (int j0 = tid - lane; j0 < nvis; j0 += 256) {
-                const int j = j0 + lane;
-                const uint32_t u = (j < nvis) ? key32[j] : 0u;
-                const bool in = (j < nvis) && ((u & mask) == prefix);
-                const unsigned active = __ballot_sync(0xffffffffu, in);
-                if (in) {
-                    const uint32_t bin = 255u - ((u >> shift) & 255u);
-                    const unsigned same = __match_any_sync(active, bin);
-                    if (lane == __ffs(same) - 1) atomicAdd(&hist[bin], (uint32_t)__popc(same));
-                }
+            for (int j = tid; j < nvis; j += 256) {
+                const uint32_t u = key32[j];
+                if ((u & mask) == prefix) atomicAdd(&whist[warp][255u - ((u >> shift) & 255u)], 1u);
+            }
+            __syncthreads();
+            {
+                uint32_t c = 0u;
+#pragma unroll
+                for (int w = 0; w < 8; ++w) c += whist[w][tid];
+                hist[tid] = c;
             }
             __syncthreads();
             if (tid < 32) {
@@ -1344,7 +1360,7 @@ int launch_select_tiles_tc(const void *Q, ugbsa_strides qs, const float *summ_a,
     rp.NBpad = P;
     rp.k_base = k_base; rp.kmax = kmax; rp.router = router ? 1 : 0;
     rp.escore = escore; rp.kv_idx = kv_idx; rp.sigma_cell = sigma_cell;
-    const size_t smem = (size_t)P * 12 + 16;
+    const size_t smem = (size_t)(P > 1024 ? P : 1024) * 8 + (size_t)P * 4 + 16;   // sort keys (>= the 8 KB of histograms) + value keys
     if (smem > 227 * 1024) return UGBSA_ERR_SHAPE;
     if (cudaFuncSetAttribute(rank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return UGBSA_ERR_LAUNCH;
