@@ -377,7 +377,6 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
     __shared__ int s_abort;
     __shared__ float s_sq[128];
     __shared__ float s_qn[128];
-    __shared__ uint32_t s_hist[2][256];
     __shared__ uint32_t s_prefix[2], s_mask[2];
     __shared__ int s_k[2];
     __shared__ uint32_t s_kmn[8], s_kmx[8];      // per-warp key range
@@ -735,33 +734,36 @@ __global__ void __launch_bounds__(kScoreThreads, 1)
                 } else {
                     int lowbit = 32 - __clz(kmn ^ kmx);   // bits below are not yet fixed
                     uint32_t prefix = (uint32_t)((unsigned long long)kmx & (~0ull << lowbit));
+                    // a histogram per warp, in the warp's own pass-2 staging area of the
+                    // envelope stages (every MMA and copy has completed; no other warp
+                    // uses that area): no cross-warp atomics, no barrier to clear it
+                    uint32_t *whist = reinterpret_cast<uint32_t *>(
+                        sK + (D <= 128 ? warp * 2 * (16 * 4 * D) : warp * 1024));
                     while (ok) {
                         const int shift = max(lowbit - 8, 0);
                         const uint32_t nb = 1u << (lowbit - shift);
                         const uint32_t himask = (uint32_t)(~0ull << lowbit);
-                        for (int i = gtid; i < 256; i += 128) s_hist[grp][i] = 0;
-                        ok = group_sync();
-                        if (!ok) break;
-                        // warp-aggregated: the lower-bound keys cluster in few bins
-                        for (int j0 = gtid - lane; j0 < nvis; j0 += 128) {
-                            const int j = j0 + lane;
-                            const uint32_t u = (j < nvis) ? tL[j] : 0u;
-                            const bool in = (j < nvis) && j != 0 && j != self_t && (u & himask) == prefix;
-                            const unsigned act = __ballot_sync(0xffffffffu, in);
-                            if (in) {
-                                const uint32_t bin = (nb - 1u) - ((u >> shift) & (nb - 1u));
-                                const unsigned same = __match_any_sync(act, bin);
-                                if (lane == __ffs(same) - 1) atomicAdd(&s_hist[grp][bin], (uint32_t)__popc(same));
-                            }
+                        for (int i = lane; i < 256; i += 32) whist[i] = 0u;
+                        __syncwarp();
+                        for (int j = gtid; j < nvis; j += 128) {
+                            const uint32_t u = tL[j];
+                            if (j != 0 && j != self_t && (u & himask) == prefix)
+                                atomicAdd(&whist[(nb - 1u) - ((u >> shift) & (nb - 1u))], 1u);
                         }
                         ok = group_sync();
                         if (!ok) break;
                         if (gtid < 32) {
+                            const uint32_t *h0 = reinterpret_cast<const uint32_t *>(
+                                sK + (D <= 128 ? (grp * 4) * 2 * (16 * 4 * D) : (grp * 4) * 1024));
+                            const int wstride = D <= 128 ? 2 * (16 * 4 * D) / 4 : 256;   // words between warps
                             uint32_t cc[8], sum = 0;
 #pragma unroll
                             for (int e = 0; e < 8; ++e) {
-                                cc[e] = s_hist[grp][8 * gtid + e];
-                                sum += cc[e];
+                                uint32_t c = 0u;
+#pragma unroll
+                                for (int w = 0; w < 4; ++w) c += h0[w * wstride + 8 * gtid + e];
+                                cc[e] = c;
+                                sum += c;
                             }
                             uint32_t incl = sum;
 #pragma unroll
