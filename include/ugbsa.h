@@ -298,7 +298,7 @@ int ugbsa_peer_buffer_free(void *ptr);
  * ugbsa_decode_attn: out [B, Hq, 1, D] = softmax over the keys (< S) of the
  *   kept blocks, fp32 accumulation, split over the kept blocks; kmax <= 1024.
  * Both take a workspace of ugbsa_decode_workspace_bytes(B, Hq, S, D, kmax)
- * bytes (one buffer serves both calls in turn).
+ * bytes (one buffer serves both calls in turn, and ugbsa_decode_step).
  */
 int ugbsa_block_summary_update(const void *K, int dtype, ugbsa_strides ks, int B, int Hkv, int S, int D, int quest,
                                int first_block, int nb_capacity, float *out_a, float *out_b, ugbsa_stream_t stream);
@@ -313,6 +313,24 @@ int ugbsa_decode_select(const void *q, int dtype, ugbsa_strides qs, const float 
 int ugbsa_decode_attn(const void *q, const void *K, const void *V, int dtype, ugbsa_strides qs, ugbsa_strides ks,
                       ugbsa_strides vs, const int32_t *kv_idx, int kmax, int B, int Hq, int Hkv, int S, int D,
                       float scale, void *out, ugbsa_strides os, void *workspace, size_t workspace_bytes,
+                      ugbsa_stream_t stream);
+
+/*
+ * ugbsa_decode_step: a whole decode step -- the same results as
+ * ugbsa_block_summary_update(first_block = ceil(S/64) - 1) + ugbsa_decode_select
+ * + ugbsa_decode_attn (kv_idx, sigma, trigger bit-identical; out identical) in
+ * three launches instead of five when B * Hq <= 256: the refresh of the cache's
+ * last block (forced in this step, so never scored) runs inside the selection
+ * after the scoring, and the router's threshold / trigger / sentinel fill run
+ * inside the attention.  summ_a / summ_b: the cache summaries (capacity
+ * nb_capacity blocks), updated in place; kv_idx [B, Hq, kmax] is written (sigma,
+ * trigger optional).  bf16 / fp16, D in {64, 128, 256}; workspace of
+ * ugbsa_decode_workspace_bytes(B, Hq, S, D, kmax) bytes.
+ */
+int ugbsa_decode_step(const void *q, const void *K, const void *V, int dtype, ugbsa_strides qs, ugbsa_strides ks,
+                      ugbsa_strides vs, float *summ_a, float *summ_b, int nb_capacity, int B, int Hq, int Hkv, int S,
+                      int D, float scale, const ugbsa_selector_config *cfg, int32_t *kv_idx, int kmax, float *sigma,
+                      uint8_t *trigger, void *out, ugbsa_strides os, void *workspace, size_t workspace_bytes,
                       ugbsa_stream_t stream);
 
 /*

@@ -146,6 +146,48 @@ def test_decode_attn_union_without_repeats():
     _check_attn(out, oracle.decode_attn(q1, k, v, kv, S, D ** -0.5))
 
 
+@pytest.mark.parametrize("case", CASES, ids=[c[0] for c in CASES])
+def test_decode_step_matches_separate_calls(case):
+    # the fused step (refresh inside the selection, router inside the attention; the
+    # separate calls past 256 cells) against refresh + decode_select + decode_attn:
+    # identical outputs, lists, margins, triggers and refreshed summaries
+    name, B, Hq, Hkv, S, D, dtype, kw = case
+    if dtype == torch.float32:
+        pytest.skip("the attention takes bf16 / fp16")
+    _, gcfg = _cfgs(kw)
+    q, k, v, _ = planted_inputs(B, Hq, Hkv, S, D, n_planted=4, seed=zlib.crc32(name.encode()) % 1000,
+                                bf16=(dtype == torch.bfloat16))
+    qd = torch.from_numpy(np.ascontiguousarray(q[:, :, -1:])).to(DEV).to(dtype)
+    kd = torch.from_numpy(k).to(DEV).to(dtype)
+    vd = torch.from_numpy(v).to(DEV).to(dtype)
+    nb = math.ceil(S / 64)
+    cap = nb + 3
+    scale = D ** -0.5
+
+    def fresh_cache():
+        a = torch.empty((B, Hkv, cap, D), device=DEV, dtype=torch.float32)
+        summ = (a, torch.empty_like(a)) if gcfg.quest else a
+        ops.block_summary_update(kd, gcfg.quest, summ, 0)
+        for t in (summ if gcfg.quest else (summ,)):   # a stale last block
+            t[:, :, nb - 1].fill_(123.0)
+        return summ
+
+    s1 = fresh_cache()
+    ops.block_summary_update(kd, gcfg.quest, s1, nb - 1)
+    kv1, sig1, trig1 = ops.decode_select(qd, s1, S, Hkv, scale, gcfg, return_router=True)
+    out1 = ops.decode_attn(qd, kd, vd, kv1, S, scale)
+    s2 = fresh_cache()
+    out2, kv2, sig2, trig2 = ops.decode_step(qd, kd, vd, s2, S, scale, gcfg, return_router=True)
+    assert torch.equal(kv1, kv2)
+    assert torch.equal(trig1, trig2)
+    a1, a2 = sig1.cpu().numpy(), sig2.cpu().numpy()
+    assert np.array_equal(np.isnan(a1), np.isnan(a2))
+    assert np.array_equal(a1[~np.isnan(a1)].view(np.uint32), a2[~np.isnan(a2)].view(np.uint32))
+    assert torch.equal(out1, out2)
+    for t1, t2 in (zip(s1, s2) if gcfg.quest else ((s1, s2),)):
+        assert torch.equal(t1[:, :, :nb], t2[:, :, :nb])
+
+
 def test_decode_with_every_block_kept_matches_sdpa():
     B, Hq, Hkv, S, D = 2, 8, 2, 5000, 128
     q, k, v, _ = planted_inputs(B, Hq, Hkv, S, D, n_planted=4, seed=12, bf16=True)

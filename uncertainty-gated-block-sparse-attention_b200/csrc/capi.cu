@@ -322,7 +322,7 @@ size_t ugbsa_decode_workspace_bytes(int B, int Hq, int S, int D, int kmax) {
     if (B <= 0 || Hq <= 0 || S <= 0 || D <= 0 || kmax <= 0) return 0;
     const size_t sel = al256s((size_t)B * Hq * 4) + al256s((size_t)B * 4) + al256s(select_finish_workspace_bytes(B, S));
     const size_t att = decode_attn_workspace_bytes(B, Hq, D, kmax);
-    return sel > att ? sel : att;
+    return sel + al256s(att);   // the fused step holds the cells' margins while the attention runs
 }
 
 int ugbsa_decode_select(const void *q, int dtype, ugbsa_strides qs, const float *summ_a, const float *summ_b,
@@ -378,6 +378,54 @@ int ugbsa_decode_attn(const void *q, const void *K, const void *V, int dtype, ug
     if (!aligned16(workspace)) return UGBSA_ERR_ALIGN;
     return launch_decode_attn(q, K, V, dtype, qs, ks, vs, kv_idx, kmax, B, Hq, Hkv, S, D, scale, out, os, workspace,
                               reinterpret_cast<cudaStream_t>(stream));
+}
+
+int ugbsa_decode_step(const void *q, const void *K, const void *V, int dtype, ugbsa_strides qs, ugbsa_strides ks,
+                      ugbsa_strides vs, float *summ_a, float *summ_b, int nb_capacity, int B, int Hq, int Hkv, int S,
+                      int D, float scale, const ugbsa_selector_config *cfg, int32_t *kv_idx, int kmax, float *sigma,
+                      uint8_t *trigger, void *out, ugbsa_strides os, void *workspace, size_t workspace_bytes,
+                      ugbsa_stream_t stream) {
+    int rc = check_cfg(cfg);
+    if (rc) return rc;
+    if (B <= 0 || Hq <= 0 || Hkv <= 0 || S <= 0 || D <= 0 || Hq % Hkv || kmax <= 0) return UGBSA_ERR_SHAPE;
+    const int NB = (S + 63) / 64;
+    if (NB > 8192 || nb_capacity < NB || kmax > 1024) return UGBSA_ERR_SHAPE;
+    if (D != 64 && D != 128 && D != 256) return UGBSA_ERR_UNSUPPORTED;
+    if (dtype != UGBSA_BF16 && dtype != UGBSA_F16) return UGBSA_ERR_DTYPE;
+    if ((rc = check_view(q, dtype, qs)) || (rc = check_view(K, dtype, ks)) || (rc = check_view(V, dtype, vs)) ||
+        (rc = check_view(out, dtype, os)))
+        return rc;
+    const bool quest = cfg_is_quest(cfg);
+    if (!kv_idx || !summ_a || (quest && !summ_b)) return UGBSA_ERR_ARG;
+    if (!aligned16(summ_a) || (quest && !aligned16(summ_b))) return UGBSA_ERR_ALIGN;
+    int kb, km;
+    budget(cfg, NB, &kb, &km);
+    if (km != kmax) return UGBSA_ERR_SHAPE;
+    if (!workspace || workspace_bytes < ugbsa_decode_workspace_bytes(B, Hq, S, D, kmax)) return UGBSA_ERR_WORKSPACE;
+    if (!aligned16(workspace)) return UGBSA_ERR_ALIGN;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const bool router = (cfg->mode == UGBSA_MODE_ROUTER) && (kb < km);
+    uint8_t *ws = static_cast<uint8_t *>(workspace);
+    float *cells = reinterpret_cast<float *>(ws);
+    const size_t sel = al256s((size_t)B * Hq * 4) + al256s((size_t)B * 4) + al256s(select_finish_workspace_bytes(B, S));
+    void *att_ws = ws + sel;
+    if ((int64_t)B * Hq <= 256) {
+        // three launches: selection (+ the last block's summary), attention (+ the router), merge
+        if ((rc = launch_decode_select(q, dtype, qs.b, qs.h, summ_a, summ_b, nb_capacity, B, Hq, Hkv, S, D, scale,
+                                       quest, kb, km, router, kv_idx, cells, st, K, ks)))
+            return rc;
+        DecodeRouter r{cfg, kb, cells, kv_idx, sigma, trigger};
+        return launch_decode_attn(q, K, V, dtype, qs, ks, vs, kv_idx, kmax, B, Hq, Hkv, S, D, scale, out, os, att_ws,
+                                  st, &r);
+    }
+    // many cells: the separate calls
+    if ((rc = ugbsa_block_summary_update(K, dtype, ks, B, Hkv, S, D, quest ? 1 : 0, NB - 1, nb_capacity, summ_a,
+                                         summ_b, stream)))
+        return rc;
+    if ((rc = ugbsa_decode_select(q, dtype, qs, summ_a, summ_b, nb_capacity, B, Hq, Hkv, S, D, scale, cfg, kv_idx,
+                                  kmax, sigma, trigger, workspace, workspace_bytes, stream)))
+        return rc;
+    return launch_decode_attn(q, K, V, dtype, qs, ks, vs, kv_idx, kmax, B, Hq, Hkv, S, D, scale, out, os, att_ws, st);
 }
 
 // ------------------------------------------------------------ norm + rotary producer

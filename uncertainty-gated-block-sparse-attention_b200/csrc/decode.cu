@@ -110,7 +110,48 @@ struct DecSelParams {
     const float *summ_a, *summ_b;
     int32_t *kv_idx;    // [B*Hq, kmax]
     float *sigma_cell;  // [B*Hq]
+    // optional refresh of the cache's last block summary (ugbsa_decode_step): K rows
+    // (K's dtype is Q's), written into summ_a / summ_b row NB - 1 after the scoring
+    const void *rK;
+    int64_t rkb, rkh, rks;
 };
+
+// Summary of block nb of K [b, kvh] (rows >= S count as 0) by the CTA's first D
+// threads from rows staged in shared memory: the canonical order of the block
+// summary kernels (mean: ((0 + k0) + k1) + ... then * 2^-6; Quest: min / max from
+// row 0 on), written to row nb of the [B, Hkv, NBs, D] summaries.
+template <typename T, bool QUEST, int D>
+__device__ void refresh_block_summary(const T *__restrict__ K, int64_t kb, int64_t kh, int64_t ks, int b, int kvh,
+                                      int Hkv, int S, int nb, int NBs, float *sa, float *sb, T *rows, int nthreads) {
+    constexpr int CH = D * (int)sizeof(T) / 16;
+    const int r_end = min(64, S - nb * 64);
+    const T *base = K + (int64_t)b * kb + (int64_t)kvh * kh + (int64_t)nb * 64 * ks;
+    for (int i = threadIdx.x; i < 64 * CH; i += nthreads) {
+        const int r = i / CH, c = i % CH;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (r < r_end) v = __ldg(reinterpret_cast<const uint4 *>(base + (int64_t)r * ks) + c);
+        reinterpret_cast<uint4 *>(rows + r * D)[c] = v;
+    }
+    __syncthreads();
+    const int d = threadIdx.x;
+    if (d < D) {
+        const int64_t o = (((int64_t)b * Hkv + kvh) * NBs + nb) * D + d;
+        if (QUEST) {
+            float mn = to_f<T>(rows[d]), mx = mn;
+            for (int r = 1; r < 64; ++r) {
+                const float x = to_f<T>(rows[r * D + d]);
+                mn = (x < mn) ? x : mn;
+                mx = (x > mx) ? x : mx;
+            }
+            sa[o] = mn;
+            sb[o] = mx;
+        } else {
+            float acc = 0.f;
+            for (int r = 0; r < 64; ++r) acc = __fadd_rn(acc, to_f<T>(rows[r * D + d]));
+            sa[o] = __fmul_rn(acc, 0.015625f);
+        }
+    }
+}
 
 template <int D> struct DecSelCfg {
     static constexpr int TR = 32;                       // summary rows per staged tile (a lane per row)
@@ -437,6 +478,15 @@ __global__ void __launch_bounds__(kDecSelThreads, 1) decode_select_kernel(const 
         }
         __syncthreads();
     }
+    // the cache's last block (forced in this step, never scored): its summary for the
+    // next steps, by the cluster's last CTA once every staged row has been read
+    if (p.rK && crank == p.CL - 1) {
+        __syncthreads();
+        refresh_block_summary<T, QUEST, D>(reinterpret_cast<const T *>(p.rK), p.rkb, p.rkh, p.rks, b, kvh, p.Hkv,
+                                           p.S, NB - 1, p.NBs, const_cast<float *>(p.summ_a),
+                                           const_cast<float *>(p.summ_b), reinterpret_cast<T *>(smem),
+                                           kDecSelThreads);
+    }
 }
 
 // One CTA over the B x Hq decode cells (B * Hq <= 1024): the router's
@@ -514,10 +564,13 @@ __global__ void __launch_bounds__(1024) decode_finish_kernel(const DecFinParams 
 
 int launch_decode_select(const void *Q, int dtype, int64_t qb, int64_t qh, const float *summ_a, const float *summ_b,
                          int NBs, int B, int Hq, int Hkv, int S, int D, float scale, bool quest, int k_base, int kmax,
-                         bool router, int32_t *kv_idx, float *sigma_cell, cudaStream_t stream) {
+                         bool router, int32_t *kv_idx, float *sigma_cell, cudaStream_t stream, const void *refresh_K,
+                         ugbsa_strides refresh_ks) {
     if (Hq / Hkv > kDecMaxGroup) return UGBSA_ERR_UNSUPPORTED;
     if (D != 64 && D != 128 && D != 256) return UGBSA_ERR_UNSUPPORTED;
-    DecSelParams p;
+    DecSelParams p = {};
+    p.rK = refresh_K;
+    p.rkb = refresh_ks.b; p.rkh = refresh_ks.h; p.rks = refresh_ks.s;
     p.B = B; p.Hq = Hq; p.Hkv = Hkv; p.G = Hq / Hkv; p.S = S; p.NB = (S + 63) / 64; p.NBs = NBs;
     // a cluster per (b, kv head): enough CTAs for the group's heads or 128 summary rows
     // each, up to 16 when the device schedules clusters of 16 (else 8)
@@ -623,7 +676,70 @@ struct DecAttnParams {
     const int32_t *kv_idx;
     float *part;   // [B*Hq, nsplit, D + 2]: o (unnormalised), m, l
     int *err;      // device error word (a wait that ran out)
+    // the router of the selection's finish, taken here (ugbsa_decode_step; B * Hq <= 256):
+    // each CTA derives its heads' triggers from the cells' margins; untriggered heads
+    // keep slots < k_base only; split 0 writes sigma / trigger and the sentinel fill
+    const float *sigma_cell;   // null: kv_idx is final
+    int router, k_base, grain_row, mode_quantile;
+    int64_t kq;
+    float tau;
+    int32_t *kv_idx_w;
+    float *sigma_out;
+    uint8_t *trigger_out;
 };
+
+// The finish's router for the G heads of group (b, kvh): bit g of the result set
+// when head g is not triggered (its slots >= k_base are dropped).  One warp; the
+// same arithmetic as decode_finish_kernel (row-grain head mean in head order,
+// the quantile's k-th smallest by counting, NaN last).
+__device__ uint32_t fused_router_untriggered(const DecAttnParams &p, int b, int kvh, int G, float *eff_out) {
+    const int lane = threadIdx.x & 31;
+    const int ncell = p.B * p.Hq;
+    if (!p.router) {   // top-k / Quest modes: no margins, nothing dropped
+        if (eff_out)
+            for (int g = 0; g < G; ++g) eff_out[g] = __int_as_float(0x7fc00000);
+        return 0u;
+    }
+    auto eff_of = [&](int bb) -> float {   // row grain: head mean of row bb
+        float acc = 0.f;
+        for (int hh = 0; hh < p.Hq; ++hh) acc = __fadd_rn(acc, p.sigma_cell[bb * p.Hq + hh]);
+        return __fdiv_rn(acc, (float)p.Hq);
+    };
+    float th = p.tau;
+    if (p.mode_quantile) {
+        const int n = p.grain_row ? p.B : ncell;
+        const int64_t kk = p.grain_row ? (p.kq - 1) / p.Hq + 1 : p.kq;
+        float found = 0.f;
+        bool got = false;
+        for (int i = lane; i < n; i += 32) {
+            const float vi = p.grain_row ? eff_of(i) : p.sigma_cell[i];
+            const uint32_t ui = asc_key_dec(vi);
+            int64_t rank = 0;
+            for (int j = 0; j < n; ++j) {
+                const float vj = p.grain_row ? eff_of(j) : p.sigma_cell[j];
+                const uint32_t uj = asc_key_dec(vj);
+                rank += (uj < ui || (uj == ui && j < i)) ? 1 : 0;
+            }
+            if (rank == kk - 1) {
+                found = (ui == 0xffffffffu) ? __int_as_float(0x7fc00000)
+                                            : __uint_as_float((ui & 0x80000000u) ? (ui & 0x7fffffffu) : ~ui);
+                got = true;
+            }
+        }
+        const unsigned who = __ballot_sync(0xffffffffu, got);
+        th = __shfl_sync(0xffffffffu, found, who ? __ffs(who) - 1 : 0);
+    }
+    uint32_t untrig = 0u;
+    const float row_eff = p.grain_row ? eff_of(b) : 0.f;
+    for (int g = 0; g < G; ++g) {
+        const int cell = b * p.Hq + kvh * G + g;
+        const float eff = p.grain_row ? row_eff : p.sigma_cell[cell];
+        const bool unc = p.mode_quantile ? (eff <= th) : (eff < th);
+        if (!unc) untrig |= 1u << g;
+        if (eff_out) eff_out[g] = eff;
+    }
+    return untrig;
+}
 
 template <typename T> struct MmaOps;
 template <> struct MmaOps<__nv_bfloat16> {
@@ -701,6 +817,7 @@ __global__ void __launch_bounds__(kDecAttnThreads) decode_group_attn_kernel(cons
     uint32_t *bm = reinterpret_cast<uint32_t *>(sQ + 16 * D * 2);
     uint32_t *entries = bm + p.G * p.NBW;
     __shared__ int s_dup, s_nent, s_abort;
+    __shared__ uint32_t s_untrig;
     __shared__ int s_wsum[kDecAttnThreads / 32];
     __shared__ __align__(8) uint64_t bar_full[STAGES];
 
@@ -737,9 +854,26 @@ __global__ void __launch_bounds__(kDecAttnThreads) decode_group_attn_kernel(cons
         for (int i = 0; i < STAGES; ++i) mbar_init(&bar_full[i], 1);
         fence_barrier_init();
     }
+    if (warp == 0) {
+        // the router (fused step): heads whose slots >= k_base are dropped
+        uint32_t untrig = 0u;
+        if (p.sigma_cell) {
+            float eff[kDecMaxGroup];
+            untrig = fused_router_untriggered(p, b, kvh, G, eff);
+            if (split == 0 && lane == 0)
+                for (int g = 0; g < G; ++g) {
+                    const int cell = cell0 + g;
+                    if (p.sigma_out) p.sigma_out[cell] = eff[g];
+                    // triggered: a router cell that kept its slots >= k_base (never without a router)
+                    if (p.trigger_out) p.trigger_out[cell] = (p.router && !((untrig >> g) & 1u)) ? 1 : 0;
+                }
+        }
+        if (lane == 0) s_untrig = untrig;
+    }
     if (use_bitmap)
         for (int i = tid; i < G * p.NBW; i += kDecAttnThreads) bm[i] = 0u;
     __syncthreads();
+    const uint32_t untrig_all = s_untrig;
     // the union of the group's lists: a bit per (head, block); a repeat marks the group.
     // The head of flat slot i is i / kmax, taken as (i + 0.5) * (1 / kmax) rounded down:
     // exact, since (i + 0.5) / kmax is at least 0.5 / kmax from an integer.
@@ -758,6 +892,7 @@ __global__ void __launch_bounds__(kDecAttnThreads) decode_group_attn_kernel(cons
                 const int blk = ids[u];
                 if (i < total && blk >= 0 && blk < p.NB) {
                     const int g = (int)(((float)i + 0.5f) * p.inv_kmax);
+                    if (((untrig_all >> g) & 1u) && i - g * p.kmax >= p.k_base) continue;   // dropped slot
                     const uint32_t bit = 1u << (blk & 31);
                     const uint32_t old = atomicOr(&bm[g * p.NBW + (blk >> 5)], bit);
                     if (old & bit) s_dup = 1;
@@ -817,13 +952,23 @@ __global__ void __launch_bounds__(kDecAttnThreads) decode_group_attn_kernel(cons
             for (int g = 0; g < kDecMaxGroup; ++g)
                 if (g < G) mask |= ((bm[g * p.NBW + w] >> bit) & 1u) << g;
         } else {
-            const int g = e / p.kmax;
-            blk = __ldg(p.kv_idx + (int64_t)(cell0 + g) * p.kmax + (e % p.kmax));
-            mask = (blk >= 0 && blk < p.NB) ? (1u << g) : 0u;
+            const int g = e / p.kmax, slot = e % p.kmax;
+            blk = __ldg(p.kv_idx + (int64_t)(cell0 + g) * p.kmax + slot);
+            const bool dropped = ((untrig_all >> g) & 1u) && slot >= p.k_base;
+            mask = (!dropped && blk >= 0 && blk < p.NB) ? (1u << g) : 0u;
         }
     };
     const int per = (nent + p.nsplit - 1) / p.nsplit;
     const int e0 = split * per, e1 = min(nent, e0 + per);
+    // the finish's sentinel fill of the untriggered heads' slots >= k_base (split 0,
+    // after its own reads; the other splits drop those slots whatever they read)
+    if (p.sigma_cell && split == 0 && untrig_all && p.kmax > p.k_base) {
+        const int w = p.kmax - p.k_base;
+        for (int i = tid; i < G * w; i += kDecAttnThreads) {
+            const int g = i / w;
+            if ((untrig_all >> g) & 1u) p.kv_idx_w[(int64_t)(cell0 + g) * p.kmax + p.k_base + i % w] = p.NB;
+        }
+    }
 
     // one thread issues a block's K and V tiles by TMA (rows past S arrive as zeros);
     // every thread waits on the stage's barrier, with a time limit
@@ -1083,8 +1228,27 @@ size_t decode_attn_workspace_bytes(int B, int Hq, int D, int kmax) {
 
 int launch_decode_attn(const void *Q, const void *K, const void *V, int dtype, ugbsa_strides qs, ugbsa_strides ks,
                        ugbsa_strides vs, const int32_t *kv_idx, int kmax, int B, int Hq, int Hkv, int S, int D,
-                       float scale, void *out, ugbsa_strides os, void *workspace, cudaStream_t stream) {
-    DecAttnParams p;
+                       float scale, void *out, ugbsa_strides os, void *workspace, cudaStream_t stream,
+                       const DecodeRouter *router) {
+    DecAttnParams p = {};
+    if (router) {
+        if ((int64_t)B * Hq > 256) return UGBSA_ERR_UNSUPPORTED;
+        const ugbsa_selector_config *cfg = router->cfg;
+        p.sigma_cell = router->sigma_cell;
+        p.router = (cfg->mode == UGBSA_MODE_ROUTER) && (router->k_base < kmax) ? 1 : 0;
+        p.k_base = router->k_base;
+        p.grain_row = cfg->router_grain == UGBSA_GRAIN_ROW ? 1 : 0;
+        p.mode_quantile = cfg->router_mode == UGBSA_ROUTER_QUANTILE ? 1 : 0;
+        const int64_t numel = (int64_t)B * Hq;
+        int64_t kq = (int64_t)(cfg->router_quantile * (double)numel);  // int(q * numel), :713-714
+        if (kq < 1) kq = 1;
+        if (kq > numel) kq = numel;
+        p.kq = kq;
+        p.tau = (float)cfg->router_tau;
+        p.kv_idx_w = router->kv_idx;
+        p.sigma_out = router->sigma_out;
+        p.trigger_out = router->trigger_out;
+    }
     p.B = B; p.Hq = Hq; p.Hkv = Hkv; p.G = Hq / Hkv; p.S = S; p.NB = (S + 63) / 64; p.kmax = kmax;
     if (p.G > kDecMaxGroup) return UGBSA_ERR_UNSUPPORTED;
     // the union is built in shared memory when its bitmaps and list fit (NB <= 8192); else slot by slot

@@ -70,18 +70,32 @@ int launch_sigma_rowsum(const float *sigma_cell, int B, int Hq, int Qt, float *r
 // decode (decode.cu): one query row per head over a cache of S keys.
 // launch_decode_select: scores + top-kmax + sigma per (b, q-head) (a cluster of CTAs per cell);
 // launch_decode_finish: the router over the B x Hq cells (B * Hq <= 1024, else UNSUPPORTED)
+// refresh_K (optional, the fused step): the cluster's last CTA also recomputes the summary of
+// the cache's last block from these K rows once the scoring has read the summaries
 int launch_decode_select(const void *Q, int dtype, int64_t qb, int64_t qh, const float *summ_a, const float *summ_b,
                          int NBs, int B, int Hq, int Hkv, int S, int D, float scale, bool quest, int k_base, int kmax,
-                         bool router, int32_t *kv_idx, float *sigma_cell, cudaStream_t stream);
+                         bool router, int32_t *kv_idx, float *sigma_cell, cudaStream_t stream,
+                         const void *refresh_K = nullptr, ugbsa_strides refresh_ks = ugbsa_strides{0, 0, 0, 0});
 int launch_decode_finish(const float *sigma_cell, int B, int Hq, int S, const ugbsa_selector_config *cfg, int k_base,
                          int kmax, int32_t *kv_idx, float *sigma_out, uint8_t *trigger_out, cudaStream_t stream);
 int launch_check_bf16_fma(const uint32_t *a, const uint32_t *b, const float *c, float *mixed, float *ref, int n,
                           cudaStream_t stream);
 int decode_nsplit(int B, int Hq, int kmax);
 size_t decode_attn_workspace_bytes(int B, int Hq, int D, int kmax);
+// the selection's router taken inside the attention (the fused step; B * Hq <= 256):
+// kv_idx as the selection left it (the attention finalises it), the cells' margins
+struct DecodeRouter {
+    const ugbsa_selector_config *cfg;
+    int k_base;
+    const float *sigma_cell;
+    int32_t *kv_idx;
+    float *sigma_out;
+    uint8_t *trigger_out;
+};
 int launch_decode_attn(const void *Q, const void *K, const void *V, int dtype, ugbsa_strides qs, ugbsa_strides ks,
                        ugbsa_strides vs, const int32_t *kv_idx, int kmax, int B, int Hq, int Hkv, int S, int D,
-                       float scale, void *out, ugbsa_strides os, void *workspace, cudaStream_t stream);
+                       float scale, void *out, ugbsa_strides os, void *workspace, cudaStream_t stream,
+                       const DecodeRouter *router = nullptr);
 
 // block-score diagnostic (select.cu): order statistics of the unforced tile scores
 // at ranks k_b, rho_k (rho_k < NB) and, if tau_hat, the noise scale (workspace:

@@ -84,6 +84,8 @@ SIGNATURES = {
                                 ctypes.POINTER(SelectorConfig), P, I, P, P, P, ctypes.c_size_t, P]),
     "ugbsa_decode_attn": (I, [P, P, P, I, Strides, Strides, Strides, P, I, I, I, I, I, I, ctypes.c_float, P, Strides,
                               P, ctypes.c_size_t, P]),
+    "ugbsa_decode_step": (I, [P, P, P, I, Strides, Strides, Strides, P, P, I, I, I, I, I, I, ctypes.c_float,
+                              ctypes.POINTER(SelectorConfig), P, I, P, P, P, Strides, P, ctypes.c_size_t, P]),
     "ugbsa_qk_norm_rope": (I, [P, I, Strides, P, I, ctypes.c_float, P, P, ctypes.c_int64, ctypes.c_int64, I, I, I,
                                I, I, P, Strides, I, P, P, P]),
     "ugbsa_select_rows_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(SelectorConfig), I, I, I]),

@@ -355,6 +355,41 @@ def decode_attn(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, kv_
     return out
 
 
+def decode_step(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, summ, S: int, scaling: float,
+                cfg: SelectorConfig, return_router: bool = False, out: torch.Tensor | None = None):
+    """One decode step (ugbsa_decode_step): the summary refresh of the cache's last
+    block, the selection and the attention -- the results of block_summary_update
+    (from the last block) + decode_select + decode_attn, in three launches.
+    query [B,Hq,1,D]; key / value [B,Hkv,>=S,D] bf16 / fp16; summ the cache
+    summaries (updated in place).  Returns out [B,Hq,1,D] (and kv_idx, sigma,
+    trigger with return_router)."""
+    _need_cuda(query, key, value)
+    B, Hq, Q, D = query.shape
+    if Q != 1 or query.dtype not in (torch.bfloat16, torch.float16) or key.dtype != query.dtype \
+            or value.dtype != query.dtype:
+        raise ValueError("decode_step takes one bf16/fp16 query row per head and K/V of its dtype")
+    Hkv = key.shape[1]
+    query, key, value = _inner_contig(query), _inner_contig(key), _inner_contig(value)
+    sa, sb = (summ if cfg.quest else (summ, None))
+    _, kmax = budget(cfg, S)
+    kv_idx = torch.empty((B, Hq, kmax), device=query.device, dtype=torch.int32)
+    sigma = torch.empty((B, Hq), device=query.device, dtype=torch.float32) if return_router else None
+    trig = torch.empty((B, Hq), device=query.device, dtype=torch.uint8) if return_router else None
+    if out is None:
+        out = torch.empty((B, Hq, 1, D), device=query.device, dtype=query.dtype)
+    ws, n = _decode_ws(B, Hq, S, D, kmax, query.device)
+    c = cfg.to_c()
+    rc = _lib.load().ugbsa_decode_step(_ptr(query), _ptr(key), _ptr(value), _DTYPES[query.dtype], _strides(query),
+                                       _strides(key), _strides(value), _ptr(sa), _ptr(sb), sa.shape[2], B, Hq, Hkv,
+                                       S, D, ctypes.c_float(scaling), ctypes.byref(c), _ptr(kv_idx), kmax,
+                                       _ptr(sigma), _ptr(trig), _ptr(out), _strides(out), _ptr(ws),
+                                       ctypes.c_size_t(n), _stream())
+    _lib.check(rc, "ugbsa_decode_step")
+    if return_router:
+        return out, kv_idx, sigma, trig.bool()
+    return out
+
+
 def qk_norm_rope(x: torch.Tensor, weight: torch.Tensor, eps: float, cos: torch.Tensor, sin: torch.Tensor,
                  norm_mode: str = "offset", out: torch.Tensor | None = None, summary: str | None = None):
     """Per-head RMSNorm + rotary embedding in one pass (ugbsa_qk_norm_rope).

@@ -967,7 +967,8 @@ def time_decode(q, k, v, cfg: ops.SelectorConfig, scale: float, reps: int = 20):
     of the last block, selection, attention) against torch SDPA over the whole
     cache (the reference's decode), CUDA events, ms per step.  Each stage is
     also captured alone in a CUDA graph and replayed, which gives its GPU time
-    without the host's per-call cost."""
+    without the host's per-call cost; fused_step_graph_ms is the same step
+    through ops.decode_step (three launches instead of five)."""
     import torch.nn.functional as F
     B, Hq, _, D = q.shape
     Hkv, S = k.shape[1], k.shape[2]
@@ -1014,6 +1015,8 @@ def time_decode(q, k, v, cfg: ops.SelectorConfig, scale: float, reps: int = 20):
     t_sel, _ = timed(lambda: ops.decode_select(q1, summ, S, Hkv, scale, cfg))
     t_att, _ = timed(lambda: ops.decode_attn(q1, k, v, kv, S, scale))
     t_graph = graphed(sparse)
+    t_step = graphed(lambda: ops.decode_step(q1, k, v, summ, S, scale, cfg)) \
+        if q1.dtype in (torch.bfloat16, torch.float16) else None
     g_refresh = graphed(refresh)
     g_sel = graphed(lambda: ops.decode_select(q1, summ, S, Hkv, scale, cfg))
     g_att = graphed(lambda: ops.decode_attn(q1, k, v, kv, S, scale))
@@ -1027,7 +1030,8 @@ def time_decode(q, k, v, cfg: ops.SelectorConfig, scale: float, reps: int = 20):
     el = k.element_size()
     union_bytes = union * 64 * D * 2 * el
     summ_bytes = B * Hkv * nb * D * 4 * (2 if cfg.quest else 1)
-    return {"sparse_ms": t_sparse, "sparse_graph_ms": t_graph, "select_ms": t_sel, "attn_ms": t_att,
+    return {"sparse_ms": t_sparse, "sparse_graph_ms": t_graph, "fused_step_graph_ms": t_step,
+            "select_ms": t_sel, "attn_ms": t_att,
             "graph_stage_ms": {"refresh": g_refresh, "select": g_sel, "attn": g_att},
             "dense_sdpa_ms": t_dense,
             "kept_blocks_per_head": kept / (B * Hq), "union_blocks_per_group": union / (B * Hkv),

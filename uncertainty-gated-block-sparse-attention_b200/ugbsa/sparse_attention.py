@@ -195,7 +195,10 @@ class SummaryCache:
     def reset(self):
         self.layers = {}
 
-    def get(self, layer_idx, key, quest: bool):
+    def get(self, layer_idx, key, quest: bool, last: bool = True):
+        """The layer's summaries, refreshed from the first block with new keys
+        (through the last block; with last=False up to the one before it, which
+        the caller refreshes itself: ops.decode_step does)."""
         B, H, S, D = key.shape
         nb = math.ceil(S / BLOCK)
         ent = self.layers.get(layer_idx)
@@ -208,8 +211,9 @@ class SummaryCache:
             ent = {"quest": quest, "shape": (B, H, D), "cap": cap, "S": 0, "summ": summ, "device": key.device}
             self.layers[layer_idx] = ent
         first = ent["S"] // BLOCK
-        if first < nb:
-            ops.block_summary_update(key, quest, ent["summ"], first)
+        upto = nb if last else nb - 1
+        if first < upto:
+            ops.block_summary_update(key[:, :, :upto * BLOCK], quest, ent["summ"], first)
         ent["S"] = S
         return ent["summ"]
 
@@ -222,9 +226,14 @@ def block_sparse_decode(module, query, key, value, scaling):
     summaries, then attention over the kept blocks.  Returns [B, 1, H, D]."""
     cfg = SEL.config()
     S = key.shape[2]
-    summ = SUMM_CACHE.get(getattr(module, "layer_idx", 0), key, cfg.quest)
-    kv_idx = ops.decode_select(query, summ, S, key.shape[1], float(scaling), cfg)
-    out = ops.decode_attn(query, key, value, kv_idx, S, float(scaling))
+    if query.dtype in (torch.bfloat16, torch.float16):
+        # blocks before the last are refreshed here; the step refreshes the last one itself
+        summ = SUMM_CACHE.get(getattr(module, "layer_idx", 0), key, cfg.quest, last=False)
+        out = ops.decode_step(query, key, value, summ, S, float(scaling), cfg)
+    else:
+        summ = SUMM_CACHE.get(getattr(module, "layer_idx", 0), key, cfg.quest)
+        kv_idx = ops.decode_select(query, summ, S, key.shape[1], float(scaling), cfg)
+        out = ops.decode_attn(query, key, value, kv_idx, S, float(scaling))
     return out.transpose(1, 2).contiguous()
 
 
