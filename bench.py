@@ -79,6 +79,12 @@ def workload(seq):
                          router_quantile=0.25, budget_blocks=max(1, nb // 32), k_min=1, k_max=max(112, nb // 32)))
 
 
+def parallel_kmax(cfg, S):
+    """kmax of the selection (the budget's second value)."""
+    from ugbsa import ops
+    return ops.budget(cfg, S)[1]
+
+
 def split_for(world, requested="auto"):
     """How a multi-GPU run divides the layer: "grid" (KV head groups x query tile
     pairs dealt round-robin), "heads" (Q heads, a KV group's split 4 + 3 when the
@@ -386,6 +392,21 @@ def run_gpu(args, seq):
         sel_fl = parallel.selection_flops(Hq, S, D)
         stages["select"]["scoring_TFLOPs"] = sel_fl / 1e12
         stages["select"]["fp32_scoring_TFLOP_s"] = sel_fl / (stages["select"]["ms"] / 1e3) / 1e12
+        # roofline on the algorithmic work: one multiply-add per (query row, visible block, d)
+        # (Quest: the same count with a sign select) against the sustained bf16 peak, and the
+        # bytes that must move (Q once, the summaries, kv_idx written), whichever bounds
+        nb_ = math.ceil(S / 64)
+        alg_fl = 2.0 * 64 * D * Hq * nb_ * (nb_ + 1) / 2
+        alg_by = (B * Hq * S * D * 2 + B * Hkv * nb_ * D * 4 * (2 if cfg.quest else 1)
+                  + B * Hq * nb_ * parallel_kmax(cfg, S) * 4)
+        pk_tf = float(peaks.get("bf16_tflops_sustained", 1399.5))
+        pk_gb = float(peaks.get("hbm_gbs", 6650.0))
+        t_fl, t_by = alg_fl / (pk_tf * 1e12), alg_by / (pk_gb * 1e9)
+        stages["select"]["roofline"] = {
+            "bound": "tensor" if t_fl >= t_by else "hbm", "algorithmic_TFLOPs": alg_fl / 1e12,
+            "algorithmic_bytes": alg_by, "roofline_ms": max(t_fl, t_by) * 1e3,
+            "frac": max(t_fl, t_by) / (stages["select"]["ms"] / 1e3),
+            "peaks": f"{pk_tf} TFLOP/s sustained bf16, {pk_gb} GB/s (measured)"}
 
     # dense denominator on the same GPU (N=1; rank 0 of a sharded run reports the 1-GPU figure)
     dense = None
