@@ -15,7 +15,9 @@
 //   attention: softmax over the keys of the kept blocks (keys < S), repeated
 //     ids counted again.
 //
-// Three launches per step (plus the summary refresh):
+// Kernels (ugbsa_decode_select / _attn: the summary refresh, the selection, the
+// router finish, the attention and the merge; ugbsa_decode_step folds the refresh
+// into the selection and the finish into the attention, three launches):
 //
 //  decode_select_kernel -- a thread-block cluster of CL CTAs per (b, kv head):
 //    CTA c stages its rows of the group's block summaries in shared memory
@@ -23,25 +25,30 @@
 //    run the canonical fp32 chains of every Q head of the group over them (a
 //    lane per row, a warp per (tile, chain) with an accumulator per head), so
 //    each summary element is read from memory and from shared memory once for
-//    the whole group.  The order keys go to the CTA that ranks
-//    the head (head g: CTA g % CL); after the cluster barrier each CTA finds its
-//    heads' kmax-th largest key by a radix selection, gathers the blocks at or
-//    above it and ranks them by counting (rank = number of candidates before it
-//    in (score desc, id asc) order), writing kv_idx[rank] and sigma.  No global
-//    handshake: two cluster barriers are the only waits.
+//    the whole group.  The order keys go to the CTA that ranks the head (head g:
+//    CTA g % CL); after the cluster barrier each CTA finds its heads' kmax-th
+//    largest key by a radix selection, gathers the blocks at or above it and
+//    ranks them by counting (rank = number of candidates before it in (score
+//    desc, id asc) order), writing kv_idx[rank] and sigma.  No global handshake:
+//    two cluster barriers are the only waits.  In the fused step the cluster's
+//    last CTA then recomputes the summary of the cache's last block (forced in
+//    this step, never scored) for the steps that follow.
 //  decode_finish_kernel -- one CTA: row-grain head mean, the quantile over the
 //    B x Hq cells by counting, the sentinel fill of the untriggered cells.
 //  decode_group_attn_kernel -- one CTA per (b, kv head, split): the union of
-//    the group's G lists (a bitmap per head; an entry = block + mask of the
-//    heads that keep it), so each kept K/V block is read once for the whole
-//    group rather than once per Q head.  The block's K and V are staged by
-//    cp.async (two or three blocks in flight); the G query rows (padded to 16) form the A
-//    operand of mma.sync m16n8k16 (16-bit inputs, fp32 accumulation): warp w
-//    takes keys 16w..16w+15 of the block, S = Q.K^T, masked to the heads of
-//    the entry, per-warp online softmax, O += P.V with P as 16-bit.  A list
-//    that repeats a block (never the selection's own lists) is processed slot
-//    by slot instead, one head per entry.  decode_combine_kernel merges the
-//    splits' partial (o, m, l).
+//    the group's G lists (a bitmap per head; the entries are the union's block
+//    ids, each block's heads read from the bitmaps when it is used), so each
+//    kept K/V block is read once for the whole group rather than once per Q
+//    head.  The block's K and V tiles arrive by TMA (128-byte swizzle, two or
+//    three blocks in flight, bounded mbarrier waits); the G query rows (padded
+//    to 16) form the A operand of mma.sync m16n8k16 (16-bit inputs, fp32
+//    accumulation): warp w takes keys 16w..16w+15 of the block, S = Q.K^T,
+//    masked to the heads of the entry, per-warp online softmax, O += P.V with P
+//    as 16-bit.  A list that repeats a block (never the selection's own lists)
+//    is processed slot by slot instead, one head per entry.  In the fused step
+//    each CTA also derives its heads' router triggers (the finish's rules) and
+//    drops the untriggered heads' slots >= k_base.  decode_combine_kernel
+//    merges the splits' partial (o, m, l).
 #include <cooperative_groups.h>
 
 #include <cfloat>
@@ -193,8 +200,10 @@ __global__ void __launch_bounds__(kDecSelThreads, 1) decode_select_kernel(const 
     float *tiles = reinterpret_cast<float *>(smem);
     uint64_t *cand = reinterpret_cast<uint64_t *>(smem);   // after the scoring, over the tiles
     const int BUFS = p.nbuf;
-    const size_t tiles_bytes = (size_t)BUFS * 2 * C::TILE_BYTES > (size_t)NB * 8 ? (size_t)BUFS * 2 * C::TILE_BYTES
-                                                                                 : (size_t)NB * 8;
+    // the candidates [NB] u64 reuse the tile buffers; the query rows after them stay 16-byte aligned
+    const size_t cand_bytes = (size_t)((NB + 1) & ~1) * 8;
+    const size_t tiles_bytes = (size_t)BUFS * 2 * C::TILE_BYTES > cand_bytes ? (size_t)BUFS * 2 * C::TILE_BYTES
+                                                                             : cand_bytes;
     float *sq = reinterpret_cast<float *>(smem + tiles_bytes);   // [NCH][G][D]
     uint32_t *keys = reinterpret_cast<uint32_t *>(sq + NCH * G * D);
     float *part = reinterpret_cast<float *>(keys + p.hpc * ((NB + 3) & ~3));   // [32 combos][2 TR rows]
@@ -620,7 +629,8 @@ int launch_decode_select(const void *Q, int dtype, int64_t qb, int64_t qh, const
         int nbuf = kDecSelMaxBufs;
         while (nbuf > 1 && (size_t)nbuf * tile + rest > budget_bytes) --nbuf;
         p.nbuf = nbuf;
-        const size_t tiles = (size_t)nbuf * tile > (size_t)p.NB * 8 ? (size_t)nbuf * tile : (size_t)p.NB * 8;
+        const size_t cand = (size_t)((p.NB + 1) & ~1) * 8;   // as the kernel lays it out
+        const size_t tiles = (size_t)nbuf * tile > cand ? (size_t)nbuf * tile : cand;
         smem = tiles + rest;
         if (smem > budget_bytes) return UGBSA_ERR_SHAPE;
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
