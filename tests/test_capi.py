@@ -200,6 +200,17 @@ def test_decode_validation_without_device():
     assert L.ugbsa_block_summary_update(fake, _lib.BF16, st, 1, 2, 4096, 128, 1, 0, 63, fake, fake, None) == 2
     assert L.ugbsa_decode_workspace_bytes(1, 28, 131072, 128, 256) >= 28 * 4
 
+    def step(nb_cap=64, kmax=km.value, ws=1 << 30, D=128, dtype=_lib.BF16, kv=fake, S=4096):
+        return L.ugbsa_decode_step(fake, fake, fake, dtype, st, st, st, fake, fake, nb_cap, 1, 8, 2, S, D,
+                                   ctypes.c_float(0.1), ctypes.byref(c), kv, kmax, None, None, fake, st, fake, ws,
+                                   None)
+    assert step(nb_cap=63) == 2       # summaries hold fewer blocks than the cache
+    assert step(kmax=km.value + 1) == 2
+    assert step(ws=16) == 6
+    assert step(D=96) == 5
+    assert step(dtype=_lib.F32) == 3  # the attention takes bf16 / fp16
+    assert step(kv=None) == 1         # kv_idx is written: required
+
 
 def test_qk_norm_rope_validation_without_device():
     L = _lib.load()

@@ -586,6 +586,8 @@ int launch_decode_select(const void *Q, int dtype, int64_t qb, int64_t qh, const
     int cl = (p.NB + 127) / 128;
     if (cl < p.G) cl = p.G;
     if (cl > 8) cl = kDecMaxCluster;
+    // many groups (a batch of sequences): clusters of 8, half the CTAs (one CTA holds an SM)
+    if ((int64_t)B * Hkv * cl > 148 && cl > 8) cl = 8;
     p.qb = qb; p.qh = qh; p.scale = scale;
     p.k_base = k_base; p.kmax = kmax; p.router = router ? 1 : 0;
     p.summ_a = summ_a; p.summ_b = summ_b; p.kv_idx = kv_idx; p.sigma_cell = sigma_cell;
@@ -699,10 +701,12 @@ struct DecAttnParams {
 };
 
 // The finish's router for the G heads of group (b, kvh): bit g of the result set
-// when head g is not triggered (its slots >= k_base are dropped).  One warp; the
-// same arithmetic as decode_finish_kernel (row-grain head mean in head order,
+// when head g is not triggered (its slots >= k_base are dropped).  One warp, on
+// the cells' margins staged in shared memory (sig [B*Hq]; row [B] is scratch);
+// the same arithmetic as decode_finish_kernel (row-grain head mean in head order,
 // the quantile's k-th smallest by counting, NaN last).
-__device__ uint32_t fused_router_untriggered(const DecAttnParams &p, int b, int kvh, int G, float *eff_out) {
+__device__ uint32_t fused_router_untriggered(const DecAttnParams &p, int b, int kvh, int G, const float *sig,
+                                             float *row, float *eff_out) {
     const int lane = threadIdx.x & 31;
     const int ncell = p.B * p.Hq;
     if (!p.router) {   // top-k / Quest modes: no margins, nothing dropped
@@ -710,11 +714,15 @@ __device__ uint32_t fused_router_untriggered(const DecAttnParams &p, int b, int 
             for (int g = 0; g < G; ++g) eff_out[g] = __int_as_float(0x7fc00000);
         return 0u;
     }
-    auto eff_of = [&](int bb) -> float {   // row grain: head mean of row bb
-        float acc = 0.f;
-        for (int hh = 0; hh < p.Hq; ++hh) acc = __fadd_rn(acc, p.sigma_cell[bb * p.Hq + hh]);
-        return __fdiv_rn(acc, (float)p.Hq);
-    };
+    if (p.grain_row) {   // the head mean of each row, once
+        for (int bb = lane; bb < p.B; bb += 32) {
+            float acc = 0.f;
+            for (int hh = 0; hh < p.Hq; ++hh) acc = __fadd_rn(acc, sig[bb * p.Hq + hh]);
+            row[bb] = __fdiv_rn(acc, (float)p.Hq);
+        }
+        __syncwarp();
+    }
+    const float *vals = p.grain_row ? row : sig;
     float th = p.tau;
     if (p.mode_quantile) {
         const int n = p.grain_row ? p.B : ncell;
@@ -722,12 +730,10 @@ __device__ uint32_t fused_router_untriggered(const DecAttnParams &p, int b, int 
         float found = 0.f;
         bool got = false;
         for (int i = lane; i < n; i += 32) {
-            const float vi = p.grain_row ? eff_of(i) : p.sigma_cell[i];
-            const uint32_t ui = asc_key_dec(vi);
+            const uint32_t ui = asc_key_dec(vals[i]);
             int64_t rank = 0;
             for (int j = 0; j < n; ++j) {
-                const float vj = p.grain_row ? eff_of(j) : p.sigma_cell[j];
-                const uint32_t uj = asc_key_dec(vj);
+                const uint32_t uj = asc_key_dec(vals[j]);
                 rank += (uj < ui || (uj == ui && j < i)) ? 1 : 0;
             }
             if (rank == kk - 1) {
@@ -740,10 +746,9 @@ __device__ uint32_t fused_router_untriggered(const DecAttnParams &p, int b, int 
         th = __shfl_sync(0xffffffffu, found, who ? __ffs(who) - 1 : 0);
     }
     uint32_t untrig = 0u;
-    const float row_eff = p.grain_row ? eff_of(b) : 0.f;
     for (int g = 0; g < G; ++g) {
         const int cell = b * p.Hq + kvh * G + g;
-        const float eff = p.grain_row ? row_eff : p.sigma_cell[cell];
+        const float eff = p.grain_row ? row[b] : sig[cell];
         const bool unc = p.mode_quantile ? (eff <= th) : (eff < th);
         if (!unc) untrig |= 1u << g;
         if (eff_out) eff_out[g] = eff;
@@ -828,6 +833,7 @@ __global__ void __launch_bounds__(kDecAttnThreads) decode_group_attn_kernel(cons
     uint32_t *entries = bm + p.G * p.NBW;
     __shared__ int s_dup, s_nent, s_abort;
     __shared__ uint32_t s_untrig;
+    __shared__ float s_sig[256], s_row[256];
     __shared__ int s_wsum[kDecAttnThreads / 32];
     __shared__ __align__(8) uint64_t bar_full[STAGES];
 
@@ -864,12 +870,16 @@ __global__ void __launch_bounds__(kDecAttnThreads) decode_group_attn_kernel(cons
         for (int i = 0; i < STAGES; ++i) mbar_init(&bar_full[i], 1);
         fence_barrier_init();
     }
+    if (p.sigma_cell) {   // the cells' margins (B * Hq <= 256), for the router below
+        for (int i = tid; i < p.B * p.Hq; i += kDecAttnThreads) s_sig[i] = p.sigma_cell[i];
+        __syncthreads();
+    }
     if (warp == 0) {
         // the router (fused step): heads whose slots >= k_base are dropped
         uint32_t untrig = 0u;
         if (p.sigma_cell) {
             float eff[kDecMaxGroup];
-            untrig = fused_router_untriggered(p, b, kvh, G, eff);
+            untrig = fused_router_untriggered(p, b, kvh, G, s_sig, s_row, eff);
             if (split == 0 && lane == 0)
                 for (int g = 0; g < G; ++g) {
                     const int cell = cell0 + g;
