@@ -41,7 +41,7 @@
 
 namespace ugbsa {
 
-template <int D>
+template <int D, int VST = 1>   // VST: V stages (two at head dim 256, where one CTA holds an SM)
 struct AttnSmem {
     static constexpr int DH = D / 64;                  // 64-column (128 B) slabs of a row
     static constexpr int Q_BYTES = DH * 64 * 128;      // [dh][64 rows][128 B]
@@ -50,7 +50,7 @@ struct AttnSmem {
     static constexpr int OFF_Q = 0;
     static constexpr int OFF_K = OFF_Q + Q_BYTES;
     static constexpr int OFF_V = OFF_K + K_BYTES;
-    static constexpr int OFF_LIST = OFF_V + V_BYTES;   // int32[kmax]
+    static constexpr int OFF_LIST = OFF_V + VST * V_BYTES;   // int32[kmax]
     // lanes 16-31: two S buffers of 128 columns; lanes 0-15: O (D columns) + P (64)
     static constexpr int TMEM_COLS = (D + 64) <= 256 ? 256 : 512;
     static_assert(2 * 128 <= TMEM_COLS && D + 64 <= TMEM_COLS, "S, O and P must fit the TMEM allocation");
@@ -157,11 +157,11 @@ __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
     return *reinterpret_cast<uint32_t *>(&v);
 }
 
-template <int D, bool BF16>
+template <int D, bool BF16, int VST = 1>
 __global__ void __launch_bounds__(kAttnThreads, (D <= 128) ? 2 : 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap mapQ, const __grid_constant__ CUtensorMap mapK,
                     const __grid_constant__ CUtensorMap mapV, const AttnParams p) {
-    using L = AttnSmem<D>;
+    using L = AttnSmem<D, VST>;
     constexpr int DH = L::DH;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -170,8 +170,8 @@ __global__ void __launch_bounds__(kAttnThreads, (D <= 128) ? 2 : 1)
     uint8_t *sV = smem + L::OFF_V;
     int32_t *sList = reinterpret_cast<int32_t *>(smem + L::OFF_LIST);
 
-    __shared__ uint64_t bar_q_full, bar_k_full, bar_k_empty, bar_v_full, bar_v_empty, bar_s_full[2], bar_p_full,
-        bar_p_free, bar_o_done;
+    __shared__ uint64_t bar_q_full, bar_k_full, bar_k_empty, bar_v_full[2], bar_v_empty[2], bar_s_full[2],
+        bar_p_full, bar_p_free, bar_o_done;
     __shared__ uint32_t s_tmem_base;
     __shared__ int s_nvalid;
     __shared__ int s_abort;
@@ -195,8 +195,10 @@ __global__ void __launch_bounds__(kAttnThreads, (D <= 128) ? 2 : 1)
         mbar_init(&bar_q_full, 1);
         mbar_init(&bar_k_full, 1);
         mbar_init(&bar_k_empty, 1);
-        mbar_init(&bar_v_full, 1);
-        mbar_init(&bar_v_empty, 1);
+        mbar_init(&bar_v_full[0], 1);
+        mbar_init(&bar_v_empty[0], 1);
+        mbar_init(&bar_v_full[1], 1);
+        mbar_init(&bar_v_empty[1], 1);
         mbar_init(&bar_s_full[0], 1);
         mbar_init(&bar_s_full[1], 1);
         mbar_init(&bar_p_full, 4);
@@ -270,17 +272,22 @@ __global__ void __launch_bounds__(kAttnThreads, (D <= 128) ? 2 : 1)
             int issued = -1;
             for (int i = 0; i < nsteps && ok; ++i) {
                 const int nb = min(2, nvalid - 2 * i);
-                ok = mbar_wait(&bar_v_empty, (i & 1) ^ 1, wc);
+                const int vs = i % VST;                            // the step's V stage and its use count
+                const uint32_t vph = (uint32_t)((i / VST) & 1);
+                ok = mbar_wait(&bar_v_empty[vs], vph ^ 1, wc);
                 if (!ok) break;
-                mbar_arrive_expect_tx(&bar_v_full, nb * 64 * D * 2);
+                mbar_arrive_expect_tx(&bar_v_full[vs], nb * 64 * D * 2);
                 for (int j = 0; j < nb; ++j) {
                     const int blk = sList[2 * i + j];
                     for (int dh = 0; dh < DH; ++dh)
-                        tma_load_4d(sV + dh * 16384 + j * 8192, &mapV, &bar_v_full, 64 * dh, blk * 64, kvh, b);
+                        tma_load_4d(sV + vs * L::V_BYTES + dh * 16384 + j * 8192, &mapV, &bar_v_full[vs], 64 * dh,
+                                    blk * 64, kvh, b);
                 }
                 issued = i;
             }
-            if (!ok && issued >= 0) mbar_wait_drain(&bar_v_full, issued & 1, p.err);
+            if (!ok)   // the copies of the last VST issued steps may still be in flight
+                for (int q = max(0, issued - VST + 1); q <= issued; ++q)
+                    mbar_wait_drain(&bar_v_full[q % VST], (uint32_t)((q / VST) & 1), p.err);
         }
     } else if (warp == 5) {
         if (lane == 0) {
@@ -311,15 +318,16 @@ __global__ void __launch_bounds__(kAttnThreads, (D <= 128) ? 2 : 1)
                 const int nb = min(2, nvalid - 2 * i);
                 ok = mbar_wait(&bar_p_full, i & 1, wc);
                 if (!ok) break;
-                ok = mbar_wait(&bar_v_full, i & 1, wc);
+                ok = mbar_wait(&bar_v_full[i % VST], (uint32_t)((i / VST) & 1), wc);
                 if (!ok) break;
                 tc_fence_after();
+                const uint32_t aVs = aV + (uint32_t)((i % VST) * L::V_BYTES);
                 for (int s = 0; s < 4 * nb; ++s) {
                     // keys 16s .. 16s+15: P columns 8s .. 8s+7
-                    const uint64_t db = smem_desc_sw128(aV + s * 2048, 16384, 1024);
+                    const uint64_t db = smem_desc_sw128(aVs + s * 2048, 16384, 1024);
                     umma_f16_ts(tO, tP + 8 * s, db, idesc_pv, (i > 0 || s > 0) ? 1u : 0u);
                 }
-                umma_commit(&bar_v_empty);
+                umma_commit(&bar_v_empty[i % VST]);
                 umma_commit(&bar_p_free);
                 if (i + 2 < nsteps) ok = issue_qk(i + 2);
             }
@@ -628,9 +636,13 @@ static int launch_attn_t(const void *Q, const void *K, const void *V, ugbsa_stri
     p.ndest = 1 + npeers;
     p.dest[0] = out;
     for (int i = 0; i < kMaxDest - 1; ++i) p.dest[i + 1] = (i < npeers) ? peers[i] : nullptr;
-    const size_t smem = (size_t)L::OFF_LIST + (size_t)kmax * 4 + 1024;
+    // head dim 256 (one CTA per SM): a second V stage when it fits, so that the next
+    // step's V blocks land while P.V runs
+    const size_t smem2 = (size_t)AttnSmem<D, 2>::OFF_LIST + (size_t)kmax * 4 + 1024;
+    const bool two_v = D > 128 && smem2 <= 227 * 1024 - 512;
+    const size_t smem = two_v ? smem2 : (size_t)L::OFF_LIST + (size_t)kmax * 4 + 1024;
     if (smem > 227 * 1024) return UGBSA_ERR_SHAPE;
-    auto kern = attn_fwd_kernel<D, BF16>;
+    auto kern = two_v ? attn_fwd_kernel<D, BF16, 2> : attn_fwd_kernel<D, BF16, 1>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return UGBSA_ERR_LAUNCH;
     const int64_t grid = (int64_t)B * Hq * p.Qt;
