@@ -75,10 +75,12 @@ struct RopeParams {
 // the block's cos / sin rows are staged in shared memory once for the group; each thread loads
 // all its rows of a head (NP independent 16-byte loads in flight) before it
 // computes them, and issues the next head's loads before storing this one's.
+// At D <= 128 the register cap (64) lets four CTAs share an SM: more loads in
+// flight per SM, for 4 bytes of spill stores and 16 of spill loads per thread.
 template <typename T, int D>
-__global__ void __launch_bounds__(256) qk_norm_rope_kernel(const T *__restrict__ X, const T *__restrict__ W,
-                                                           const T *__restrict__ Cs, const T *__restrict__ Sn,
-                                                           T *Y, const RopeParams p) {
+__global__ void __launch_bounds__(256, (D <= 128) ? 4 : 2)
+    qk_norm_rope_kernel(const T *__restrict__ X, const T *__restrict__ W, const T *__restrict__ Cs,
+                        const T *__restrict__ Sn, T *Y, const RopeParams p) {
     constexpr int TPR = D / 8;          // threads per row
     constexpr int RPP = 256 / TPR;      // rows per pass
     constexpr int NP = 64 / RPP;        // passes per 64-row block
