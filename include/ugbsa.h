@@ -294,7 +294,8 @@ int ugbsa_peer_buffer_free(void *ptr);
  *   (descending score, ties to the lower id; kmax from ugbsa_select_budget at
  *   S), and applies the router over the B x Hq cells (one tile per cell):
  *   kv_idx [B, Hq, kmax] with sentinel NB in the untriggered cells' slots
- *   >= k_base; sigma / trigger [B, Hq] optional.
+ *   >= k_base; sigma / trigger [B, Hq] optional.  S <= 524288 (8192 blocks),
+ *   D in {64, 128, 256}, at most 16 Q heads per KV head.
  * ugbsa_decode_attn: out [B, Hq, 1, D] = softmax over the keys (< S) of the
  *   kept blocks, fp32 accumulation, split over the kept blocks; kmax <= 1024.
  * Both take a workspace of ugbsa_decode_workspace_bytes(B, Hq, S, D, kmax)
