@@ -194,6 +194,11 @@ __device__ __forceinline__ uint64_t fadd_x2(uint64_t a, uint64_t b) {
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
     return d;
 }
+__device__ __forceinline__ uint64_t fmul_x2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
 
 // Barrier over a subset of the CTA's warps (id 1..15; __syncthreads uses 0).
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {

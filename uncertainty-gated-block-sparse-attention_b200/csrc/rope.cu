@@ -76,7 +76,7 @@ struct RopeParams {
 // all its rows of a head (NP independent 16-byte loads in flight) before it
 // computes them, and issues the next head's loads before storing this one's.
 // At D <= 128 the register cap (64) lets four CTAs share an SM: more loads in
-// flight per SM, for 4 bytes of spill stores and 16 of spill loads per thread.
+// flight per SM.  The fp32 element work runs on packed pairs (mul / add .f32x2).
 template <typename T, int D>
 __global__ void __launch_bounds__(256, (D <= 128) ? 4 : 2)
     qk_norm_rope_kernel(const T *__restrict__ X, const T *__restrict__ W, const T *__restrict__ Cs,
@@ -164,29 +164,41 @@ __global__ void __launch_bounds__(256, (D <= 128) ? 4 : 2)
                     x[2 * i + 1] = f.y;
                 }
             }
-            float ss = 0.f;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) ss = __fadd_rn(ss, __fmul_rn(x[i], x[i]));   // x^2 rounded, as pow(2)
-#pragma unroll
-            for (int off = TPR >> 1; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-            // D is a power of two: the mean's division is an exact scaling
-            const float rs = 1.0f / sqrtf(__fadd_rn(__fmul_rn(ss, 1.0f / (float)D), p.eps));
             uint32_t yv[4];
-            const uint32_t xw[4] = {xa[ps].x, xa[ps].y, xa[ps].z, xa[ps].w};
+            if (p.norm_mode == 2) {   // no norm: the input pairs as they are
+                yv[0] = xa[ps].x; yv[1] = xa[ps].y; yv[2] = xa[ps].z; yv[3] = xa[ps].w;
+            } else {
+                // x^2 rounded (as pow(2)), then summed: packed fp32 pairs, the even and the
+                // odd columns in the two halves, joined at the end
+                uint64_t sq = 0;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                T2 v;
-                if (p.norm_mode == 2) {
-                    yv[i] = xw[i];   // no norm: the input pairs as they are
-                    continue;
+                for (int i = 0; i < 4; ++i) {
+                    const uint64_t v = f32x2(x[2 * i], x[2 * i + 1]);
+                    sq = (i == 0) ? fmul_x2(v, v) : fadd_x2(sq, fmul_x2(v, v));
                 }
-                if (p.norm_mode == 1) {
-                    v = to_pair<T2>(__fmul_rn(__fmul_rn(x[2 * i], rs), w1[2 * i]),
-                                    __fmul_rn(__fmul_rn(x[2 * i + 1], rs), w1[2 * i + 1]));
-                } else {
-                    v = __hmul2_rn(w2[i], to_pair<T2>(__fmul_rn(x[2 * i], rs), __fmul_rn(x[2 * i + 1], rs)));
+                float se, so;
+                f32x2_split(sq, se, so);
+                float ss = __fadd_rn(se, so);
+#pragma unroll
+                for (int off = TPR >> 1; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+                // D is a power of two: the mean's division is an exact scaling; 1 / sqrt as
+                // two correctly rounded steps
+                const float rs = __frcp_rn(__fsqrt_rn(__fadd_rn(__fmul_rn(ss, 1.0f / (float)D), p.eps)));
+                const uint64_t rs2 = f32x2(rs, rs);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    float n0, n1;
+                    f32x2_split(fmul_x2(f32x2(x[2 * i], x[2 * i + 1]), rs2), n0, n1);
+                    T2 v;
+                    if (p.norm_mode == 1) {
+                        float a0, a1;
+                        f32x2_split(fmul_x2(f32x2(n0, n1), f32x2(w1[2 * i], w1[2 * i + 1])), a0, a1);
+                        v = to_pair<T2>(a0, a1);
+                    } else {
+                        v = __hmul2_rn(w2[i], to_pair<T2>(n0, n1));
+                    }
+                    yv[i] = *reinterpret_cast<uint32_t *>(&v);
                 }
-                yv[i] = *reinterpret_cast<uint32_t *>(&v);
             }
             uint32_t yp[4];   // the rotary partner columns
 #pragma unroll
