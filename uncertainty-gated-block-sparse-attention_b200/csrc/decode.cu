@@ -215,17 +215,6 @@ __global__ void __launch_bounds__(kDecSelThreads, 1) decode_select_kernel(const 
     grid_dep_launch();
     grid_dep_wait();   // the summaries (a refresh just before) are complete
 
-    // the group's query rows: Quest max(q,0) and min(q,0); mean q
-    for (int i = tid; i < G * D; i += kDecSelThreads) {
-        const int g = i / D, d = i % D;
-        const float x = to_f<T>(Q[(int64_t)b * p.qb + (int64_t)(kvh * G + g) * p.qh + d]);
-        if (QUEST) {
-            sq[i] = x > 0.f ? x : 0.f;
-            sq[G * D + i] = x < 0.f ? x : 0.f;
-        } else {
-            sq[i] = x;
-        }
-    }
     // the rows of this CTA: [r0, r1), staged by cp.async in rounds of two TR-row tiles
     const int r0 = crank * p.chunk, r1 = min(NB, r0 + p.chunk);
     constexpr int RR = 2 * C::TR;                           // rows per round (a lane runs two chains)
@@ -253,8 +242,18 @@ __global__ void __launch_bounds__(kDecSelThreads, 1) decode_select_kernel(const 
         if (rd < nrounds) stage(rd);
         else cp_async_commit();
     }
-    // every CTA of the cluster is running before any writes another's shared memory
-    cluster.sync();
+    // the group's query rows (while the first rows are in flight): Quest max(q,0) and
+    // min(q,0); mean q
+    for (int i = tid; i < G * D; i += kDecSelThreads) {
+        const int g = i / D, d = i % D;
+        const float x = to_f<T>(Q[(int64_t)b * p.qb + (int64_t)(kvh * G + g) * p.qh + d]);
+        if (QUEST) {
+            sq[i] = x > 0.f ? x : 0.f;
+            sq[G * D + i] = x < 0.f ? x : 0.f;
+        } else {
+            sq[i] = x;
+        }
+    }
 
     // chains: warp w < 2 * NCH takes tile w / NCH of the round and chain w % NCH for
     // every head of the group (up to GM fma chains per lane, one row per lane): each
@@ -291,6 +290,9 @@ __global__ void __launch_bounds__(kDecSelThreads, 1) decode_select_kernel(const 
                 if (g < G) part[(g * NCH + ch) * RR + tt * C::TR + lane] = acc[g];
         }
         __syncthreads();
+        // every CTA of the cluster is running before any writes another's shared memory
+        // (taken once per thread: here in round 0, or below by a CTA without rows)
+        if (rd == 0) cluster.sync();
         // score -> order key, into the owner CTA of the head (sink and own block forced)
         const int rb = r0 + rd * RR;
         for (int i = tid; i < G * RR; i += kDecSelThreads) {
@@ -311,6 +313,7 @@ __global__ void __launch_bounds__(kDecSelThreads, 1) decode_select_kernel(const 
             dk[(size_t)(g / p.CL) * ((NB + 3) & ~3) + j] = u;
         }
     }
+    if (nrounds == 0) cluster.sync();   // the first barrier, for a CTA without rows
     cp_async_wait_all();
     cluster.sync();   // every key is with its head's CTA
 
