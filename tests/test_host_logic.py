@@ -58,6 +58,37 @@ def test_hook_rejects_out_of_scope_modes():
         sa.SEL.mode, sa.SEL.kernel_v2 = old
 
 
+def test_sparse_decode_domain():
+    bf = torch.bfloat16
+    assert sa.sparse_decode_supported(torch.zeros(1, 8, 1, 128, dtype=bf), torch.zeros(1, 2, 4096, 128, dtype=bf))
+    # fp32, head dim 96, 32 Q heads per KV head, more than 8192 blocks: outside it
+    assert not sa.sparse_decode_supported(torch.zeros(1, 8, 1, 128), torch.zeros(1, 2, 4096, 128))
+    assert not sa.sparse_decode_supported(torch.zeros(1, 8, 1, 96, dtype=bf), torch.zeros(1, 2, 4096, 96, dtype=bf))
+    assert not sa.sparse_decode_supported(torch.zeros(1, 32, 1, 64, dtype=bf), torch.zeros(1, 1, 4096, 64, dtype=bf))
+    assert not sa.sparse_decode_supported(torch.zeros(1, 2, 1, 64, dtype=bf),
+                                          torch.zeros(1, 1, 8192 * 64 + 1, 64, dtype=bf))
+
+
+def test_hook_decodes_densely_outside_the_sparse_decode_domain():
+    # an fp32 decode row with SEL.decode_sparse set: the reference's dense SDPA decode
+    class M:
+        layer_idx = 0
+        num_key_value_groups = 2
+    old = sa.SEL.mode, sa.SEL.kernel_v2, sa.SEL.decode_sparse
+    try:
+        sa.SEL.mode, sa.SEL.kernel_v2, sa.SEL.decode_sparse = "router", True, True
+        g = torch.Generator().manual_seed(3)
+        q = torch.randn(1, 4, 1, 64, generator=g)
+        k = torch.randn(1, 2, 300, 64, generator=g)
+        v = torch.randn(1, 2, 300, 64, generator=g)
+        out, _ = sa.block_sparse_attention(M(), q, k, v, None, 0.125)
+        want = torch.nn.functional.scaled_dot_product_attention(q, k, v, scale=0.125, enable_gqa=True)
+        assert out.shape == (1, 1, 4, 64)
+        assert torch.allclose(out, want.transpose(1, 2), atol=1e-6)
+    finally:
+        sa.SEL.mode, sa.SEL.kernel_v2, sa.SEL.decode_sparse = old
+
+
 def test_selected_block_flops_counts_usable_slots():
     S, D = 256, 128
     nb = 4

@@ -221,19 +221,25 @@ class SummaryCache:
 SUMM_CACHE = SummaryCache()
 
 
+def sparse_decode_supported(query, key) -> bool:
+    """The block-sparse decode's domain (ugbsa_decode_step): 16-bit Q / K / V,
+    head dim 64 / 128 / 256, at most 16 Q heads per KV head, caches of at most
+    8192 blocks (512K tokens).  Outside it the hook decodes densely, as the
+    reference always does."""
+    Hq, Hkv, S, D = query.shape[1], key.shape[1], key.shape[2], query.shape[-1]
+    return (query.dtype in (torch.bfloat16, torch.float16) and key.dtype == query.dtype and D in (64, 128, 256)
+            and Hq % Hkv == 0 and Hq // Hkv <= 16 and S <= 8192 * 64)
+
+
 def block_sparse_decode(module, query, key, value, scaling):
-    """One decode row per head over the cache: block selection on the cached
-    summaries, then attention over the kept blocks.  Returns [B, 1, H, D]."""
+    """One decode row per head over the cache (bf16 / fp16, see
+    sparse_decode_supported): block selection on the cached summaries, then
+    attention over the kept blocks.  Returns [B, 1, H, D]."""
     cfg = SEL.config()
     S = key.shape[2]
-    if query.dtype in (torch.bfloat16, torch.float16):
-        # blocks before the last are refreshed here; the step refreshes the last one itself
-        summ = SUMM_CACHE.get(getattr(module, "layer_idx", 0), key, cfg.quest, last=False)
-        out = ops.decode_step(query, key, value, summ, S, float(scaling), cfg)
-    else:
-        summ = SUMM_CACHE.get(getattr(module, "layer_idx", 0), key, cfg.quest)
-        kv_idx = ops.decode_select(query, summ, S, key.shape[1], float(scaling), cfg)
-        out = ops.decode_attn(query, key, value, kv_idx, S, float(scaling))
+    # blocks before the last are refreshed here; the step refreshes the last one itself
+    summ = SUMM_CACHE.get(getattr(module, "layer_idx", 0), key, cfg.quest, last=False)
+    out = ops.decode_step(query, key, value, summ, S, float(scaling), cfg)
     return out.transpose(1, 2).contiguous()
 
 
@@ -242,7 +248,8 @@ def block_sparse_attention(module, query, key, value, attention_mask, scaling, d
     v2 sparse path.  Returns ``(attn_output [B, S, H, D] contiguous, None)``."""
     Q = query.shape[-2]
     is_prefill = Q > 1
-    if Q == 1 and SEL.decode_sparse and SEL.kernel_v2 and SEL.mode in ("topk", "router", "quest"):
+    if Q == 1 and SEL.decode_sparse and SEL.kernel_v2 and SEL.mode in ("topk", "router", "quest") \
+            and sparse_decode_supported(query, key):
         return block_sparse_decode(module, query, key, value, scaling), None
     if SEL.mode == "dense" or Q == 1:
         ev = PROF.start("dense_sdpa") if is_prefill else None
