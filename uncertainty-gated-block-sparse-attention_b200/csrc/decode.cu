@@ -291,7 +291,7 @@ __global__ void __launch_bounds__(kDecSelThreads, 1) decode_select_kernel(const 
         }
         __syncthreads();
         // every CTA of the cluster is running before any writes another's shared memory
-        // (taken once per thread: here in round 0, or below by a CTA without rows)
+        // (taken once per thread: here in the first staged round, or below by a CTA without rows)
         if (rd == 0) cluster.sync();
         // score -> order key, into the owner CTA of the head (sink and own block forced)
         const int rb = r0 + rd * RR;
